@@ -1,0 +1,164 @@
+/*
+ * mogemma_b200.h -- C ABI of libmogemma_cuda.so, the B200 (sm_100a) Gemma 3
+ * forward/decode engine that replaces the MoGemma Mojo engine behind the
+ * `mogemma._core` operator boundary.
+ *
+ * Conventions
+ *   - Every entry point returns mg_status; on failure mg_last_error() returns a
+ *     thread-local message.  Messages that the reference raises keep its wording
+ *     ("Sequence length exceeded", core.mojo:380-381).
+ *   - Pointers named *_host are host memory owned by the caller; the library
+ *     copies them in or out on the model's stream and synchronises before it
+ *     returns.  Device memory (weights, KV cache, activations) is owned by the
+ *     model and freed by mg_model_destroy.
+ *   - Not re-entrant per model handle (the reference's `llm` dict is not either,
+ *     src/py/mogemma/model.py:341-345); different handles may be used from
+ *     different host threads.
+ *
+ * Reference interfaces replaced (paths inside the cofin/mogemma project):
+ *   mg_model_create   <- init_model_mojo          src/mo/mogemma/core.mojo:274-364
+ *   mg_model_info     <- the init_model dict keys  src/mo/mogemma/core.mojo:350-364
+ *   mg_set_pos        <- llm["pos"] = 0            src/py/mogemma/model.py:341-342
+ *   mg_step           <- step_mojo                 src/mo/mogemma/core.mojo:366-461
+ *                        + _sample_next_token      src/py/mogemma/model.py:103-150
+ *   mg_prefill        <- the prefill step loop     src/py/mogemma/model.py:344-345
+ *   mg_generate       <- the decode step loop      src/py/mogemma/model.py:354-371
+ *   mg_sample         <- _sample_next_token        src/py/mogemma/model.py:103-150
+ *   mg_embed          <- generate_embeddings_mojo  src/mo/mogemma/core.mojo:463-600
+ */
+#ifndef MOGEMMA_B200_H
+#define MOGEMMA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MG_ABI_VERSION 1
+
+typedef enum mg_status {
+    MG_OK = 0,
+    MG_ERR_INVALID = 1,      /* bad argument or inconsistent weights */
+    MG_ERR_CUDA = 2,         /* a CUDA runtime call failed */
+    MG_ERR_OOM = 3,          /* device allocation failed */
+    MG_ERR_SEQ_EXCEEDED = 4, /* pos >= capacity: "Sequence length exceeded" */
+    MG_ERR_TIMEOUT = 5,      /* a bounded device-side wait expired (kernel returned early) */
+    MG_ERR_UNSUPPORTED = 6,  /* configuration not built into this library */
+    MG_ERR_NCCL = 7          /* a collective failed or timed out */
+} mg_status;
+
+typedef enum mg_dtype {
+    MG_F32 = 0,
+    MG_BF16 = 1,
+    MG_F16 = 2,
+    MG_I32 = 3,
+    MG_U8 = 4,
+    MG_OTHER = 99
+} mg_dtype;
+
+/* One weight tensor as the reference loader hands it over: a borrowed host
+ * pointer into the safetensors mmap plus shape (src/py/mogemma/loader.py:86-107).
+ * Names are the HF names listed in core.mojo:79-104. */
+typedef struct mg_tensor_desc {
+    const char *name;
+    const void *data;
+    int64_t shape[4];
+    int32_t ndim;
+    int32_t dtype; /* mg_dtype of `data` */
+} mg_tensor_desc;
+
+typedef struct mg_options {
+    int32_t struct_size;      /* sizeof(mg_options) */
+    int32_t device;           /* CUDA device ordinal */
+    int32_t mode;             /* 0: reference semantics; 1: gemma3 (window + dual theta) */
+    int32_t weight_dtype;     /* device storage of projection weights: MG_F32 or MG_BF16 */
+    int32_t max_batch;        /* decode rows held in the KV cache */
+    int32_t capacity;         /* KV positions per row (reference: 8192, core.mojo:328) */
+    int32_t sliding_window;   /* gemma3 mode: local-layer window */
+    int32_t global_every;     /* gemma3 mode: layer l is global iff (l+1) % global_every == 0 */
+    float rope_theta_local;   /* gemma3 mode */
+    float rope_theta_global;  /* gemma3 mode */
+    uint64_t seed;            /* sampler Philox seed */
+    void *stream;             /* cudaStream_t to run on; NULL: the library creates one */
+    int32_t decode_path;      /* 0: persistent decode kernel; 1: one launch per phase */
+    int32_t tp_rank;          /* tensor-parallel rank (0 when tp_size == 1) */
+    int32_t tp_size;          /* tensor-parallel degree */
+    int32_t reserved0;
+    const void *nccl_id;      /* 128-byte ncclUniqueId when tp_size > 1 */
+} mg_options;
+
+typedef struct mg_model_info {
+    int32_t num_layers, num_heads, num_kv_heads, head_dim;
+    int32_t hidden_size, intermediate_size, vocab_size, max_seq_len;
+    int32_t max_batch, mode, weight_dtype, tp_size;
+    int64_t weight_bytes_per_step; /* projection + lm_head bytes streamed per decode step */
+    int64_t kv_bytes_per_pos;      /* K+V bytes per cached position, all layers, one row */
+    int32_t num_sms, persistent_ctas;
+} mg_model_info;
+
+/* Sampling controls of GenerationConfig (src/py/mogemma/config.py:63-69).
+ * temperature/top_p are doubles because the reference divides float64 logits
+ * by the Python float (model.py:105,113). */
+typedef struct mg_sampling {
+    double temperature; /* <= 0: greedy argmax (first maximum) */
+    int32_t top_k;      /* 0 or >= vocab: no top-k filter */
+    int32_t reserved0;
+    double top_p;       /* (0,1): nucleus filter; otherwise off */
+    const double *uniforms_host; /* optional [batch] draw variates in [0,1); NULL: Philox stream */
+} mg_sampling;
+
+typedef struct mg_model mg_model;
+
+/* ---- library ---- */
+const char *mg_last_error(void);
+int32_t mg_abi_version(void);
+
+/* ---- model lifetime ---- */
+mg_status mg_model_create(const mg_tensor_desc *descs, int32_t n, const mg_options *opt, mg_model **out);
+mg_status mg_model_info_get(const mg_model *m, mg_model_info *info);
+mg_status mg_model_destroy(mg_model *m);
+/* The cudaStream_t the model runs on (for event timing by the caller). */
+void *mg_model_stream(const mg_model *m);
+
+/* ---- positions (per batch row) ---- */
+mg_status mg_set_pos(mg_model *m, int32_t row, int32_t pos); /* row -1: every row */
+mg_status mg_get_pos(const mg_model *m, int32_t *pos_host, int32_t n);
+
+/* ---- decode ----
+ * One forward step for rows [0, batch): feeds token_ids_host[b] at that row's
+ * position, writes its K/V, advances its position.  logits_host (nullable) gets
+ * [batch, vocab] fp32 logits; sampled_host (nullable, needs s) gets one token per
+ * row drawn by the _sample_next_token rules. */
+mg_status mg_step(mg_model *m, const int32_t *token_ids_host, int32_t batch, float *logits_host,
+                  int32_t *sampled_host, const mg_sampling *s);
+/* Prefill: for each row b, feeds lens_host[b] tokens (row-major, stride max_len)
+ * without computing logits, exactly like the reference's prefill loop that
+ * discards step() outputs.  Positions advance by lens_host[b]. */
+mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
+                     int32_t max_len);
+/* Device-resident decode loop: n_steps steps; each step's input is the previous
+ * step's sampled token (the first step uses the token set by the last mg_step /
+ * mg_set_tokens).  tokens_host (nullable) receives [n_steps, batch] ids after the
+ * loop; with NULL nothing is copied back. */
+mg_status mg_generate(mg_model *m, int32_t n_steps, int32_t batch, const mg_sampling *s, int32_t *tokens_host);
+mg_status mg_set_tokens(mg_model *m, const int32_t *token_ids_host, int32_t batch);
+
+/* ---- sampling over caller logits ---- */
+mg_status mg_sample(const float *logits_host, int32_t batch, int32_t vocab, const mg_sampling *s, uint64_t seed,
+                    uint64_t offset, int32_t *out_host);
+
+/* ---- embeddings ----
+ * Mean of final-normed hidden states per sequence (forward_sequence,
+ * layers.mojo:292-370), ids row-major [batch, max_len] with lens_host[b] valid. */
+mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
+                   int32_t max_len, float *out_host);
+
+/* ---- inspection (tests) ---- */
+mg_status mg_read_kv(const mg_model *m, int32_t layer, int32_t row, int32_t pos, float *k_host, float *v_host);
+mg_status mg_nccl_unique_id(void *out128);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

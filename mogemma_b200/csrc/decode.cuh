@@ -1,0 +1,99 @@
+// decode.cuh -- parameter block and constants of the persistent decode kernel.
+//
+// One launch runs a contiguous range of "phases" of a decode step for B rows:
+//   per layer l: QKV(l), ATT(l), O(l), GU(l), D(l); then LMH, then SAMPLE.
+// Each CTA is split into 8 consumer warps and 1 producer warp.  The producer
+// streams this CTA's weight tiles (and past K/V rows) through a ring of
+// shared-memory stages with 1-D bulk async copies, running ahead across phase
+// boundaries because weights never depend on activations.  Consumers wait on
+// gpu-scope phase counters for the activations of the previous phase.
+#pragma once
+
+#include <stdint.h>
+
+namespace mg {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kStageBytes = 36864;   // one ring stage
+constexpr int kMaxRows = 8;          // batch rows per persistent launch
+constexpr int kMaxHeadDim = 256;
+constexpr int kMaxQPerKv = 8;
+constexpr int kMaxTopK = 64;         // fused top-k width
+constexpr int kAttTile = 16;         // positions per attention tile
+
+enum PhaseKind : int { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_D = 4, PH_LMH = 5, PH_SAMPLE = 6 };
+
+// lm_mode
+constexpr int kLmNone = 0;    // no lm_head (prefill tokens whose logits are discarded)
+constexpr int kLmLogits = 1;  // logits (+ fused top-k candidates when topk > 0)
+constexpr int kLmEmbed = 2;   // accumulate final-normed state into emb_acc
+
+struct LayerPtrs {
+    const void *qkv;   // [qkv_rows][Hp]   rows: q (Hq*hd), k (Hkv*hd), v (Hkv*hd)
+    const void *o;     // [H][Ap]
+    const void *gate;  // [I][Hp]
+    const void *up;    // [I][Hp]
+    const void *down;  // [H][Ip]
+    const float *in_ln, *post_attn_ln, *pre_ff_ln, *post_ff_ln;  // [H]
+    const float *q_norm, *k_norm;                                // [hd] or null
+    int32_t is_global;
+    int32_t pad_;
+};
+
+struct DecodeParams {
+    // dimensions (padded row lengths are multiples of 128 elements)
+    int32_t L, H, Hp, Hq, Hkv, hd, hdp, I, Ip, V, A, Ap, qkv_rows;
+    int32_t B;        // rows in this launch
+    int32_t cap;      // KV positions per row
+    int32_t window;   // local-layer window (gemma3 mode), 0 = unbounded
+    int32_t S;        // ring stages
+    int32_t att_ch;   // positions per attention chunk (multiple of kAttTile)
+    int32_t max_ch;   // chunks allocated per (row, kv head)
+    int32_t lm_mode;
+    int32_t topk;     // fused candidates per row (0: none, 1: argmax, <= kMaxTopK)
+    int32_t ph_begin, ph_end;
+    int32_t xs_floats;  // floats reserved for the activation stage in shared memory
+    int32_t step_t;     // token index within mg_prefill/mg_embed (row active iff step_t < nvalid[b])
+    int32_t ids_ld;
+    int32_t pad0_;
+
+    const LayerPtrs *layers;
+    const void *lm_head;   // [V][Hp]
+    const void *embed;     // [V][embed_ld]
+    int64_t embed_ld;
+    const float *final_norm;
+    const float *rope_cos_l, *rope_sin_l, *rope_cos_g, *rope_sin_g;  // [cap][hd/2]
+    float *kc, *vc;                                                   // [L][Bmax][Hkv][cap][hdp]
+    int64_t kv_layer_stride, kv_row_stride, kv_head_stride;
+
+    float *h, *r, *qkv, *o_raw, *act, *mlp_raw;  // [B][...] activations
+    float *attn_part, *attn_out;
+    float *logits;      // [B][V]
+    uint64_t *cand_key; // [B][G][kMaxTopK] per-CTA top-k keys of the lm_head rows
+    float *emb_acc;     // [B][H]
+
+    int32_t *tok;            // [B] current input token per row
+    int32_t *pos;            // [B] position of the next token per row
+    const int32_t *ids;      // optional [B][ids_ld] token matrix (prefill / embed)
+    const int32_t *nvalid;   // optional [B] valid tokens per row
+    int32_t *out_tokens;     // optional [B] sampled tokens of this step
+
+    // sampling
+    double temperature, top_p;
+    int32_t top_k_req;   // the caller's top_k (reference semantics)
+    int32_t sample;      // 1: draw a token per row in PH_SAMPLE
+    const double *uniforms;  // optional [B]
+    uint64_t seed;
+    uint64_t rng_offset;     // Philox counter of this step's draws
+
+    uint32_t *sync;   // phase counters [n_phases], att_done [L], att_cnt [B*Hkv], exit [1]
+    uint32_t *err;    // device error word
+    int32_t n_phases;
+    int32_t pad1_;
+};
+
+inline int num_phases(int L) { return 5 * L + 2; }
+
+}  // namespace mg

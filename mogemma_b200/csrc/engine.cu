@@ -1,0 +1,893 @@
+// engine.cu -- host side of libmogemma_cuda: the C ABI declared in
+// include/mogemma_b200.h (model creation, weight upload, decode launches,
+// prefill, embeddings, sampling, inspection).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/mogemma_b200.h"
+#include "common.cuh"
+#include "decode.cuh"
+
+namespace mg {
+size_t decode_smem_bytes(int S, int xs_floats);
+template <typename WT>
+size_t decode_static_smem();
+template <typename WT>
+cudaError_t decode_prepare(size_t dynamic_smem);
+template <typename WT>
+int decode_occupancy(size_t smem);
+template <typename WT>
+cudaError_t decode_launch(const DecodeParams &p, int grid, size_t smem, cudaStream_t stream, bool cooperative);
+size_t sample_rows_smem();
+cudaError_t sample_rows_launch(const float *logits, int64_t ld, int rows, int V, double temperature, int top_k,
+                               double top_p, const double *uniforms, uint64_t seed, uint64_t offset, int32_t *out,
+                               int32_t *tok, cudaStream_t stream);
+cudaError_t convert_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, void *dst, int dst_dtype,
+                                int64_t dst_ld, cudaStream_t stream);
+}  // namespace mg
+
+using namespace mg;
+
+// ---------------------------------------------------------------- errors
+static thread_local std::string g_err;
+
+static mg_status fail(mg_status st, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return st;
+}
+
+#define CU(call)                                                                                       \
+    do {                                                                                               \
+        cudaError_t e_ = (call);                                                                       \
+        if (e_ != cudaSuccess)                                                                         \
+            return fail(e_ == cudaErrorMemoryAllocation ? MG_ERR_OOM : MG_ERR_CUDA, "%s failed: %s (%s:%d)", \
+                        #call, cudaGetErrorString(e_), __FILE__, __LINE__);                            \
+    } while (0)
+
+#define TRY(expr)                      \
+    do {                               \
+        mg_status s_ = (expr);         \
+        if (s_ != MG_OK) return s_;    \
+    } while (0)
+
+extern "C" const char *mg_last_error(void) { return g_err.c_str(); }
+extern "C" int32_t mg_abi_version(void) { return MG_ABI_VERSION; }
+
+// ---------------------------------------------------------------- model
+struct mg_model {
+    int dev = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    int mode = 0, wdtype = MG_F32, decode_path = 0;
+    int L = 0, H = 0, Hq = 0, Hkv = 0, hd = 0, I = 0, V = 0, cap = 8192, Bmax = 1;
+    int Hp = 0, Ap = 0, Ip = 0, hdp = 0, qkv_rows = 0, A = 0;
+    int window = 0, global_every = 1;
+    float theta_l = 10000.f, theta_g = 10000.f;
+    uint64_t seed = 0, rng_offset = 0;
+    int num_sms = 0, G = 0, S = 0, xs_floats = 0, max_ch = 0;
+    size_t smem = 0;
+    int64_t weight_bytes = 0;
+
+    std::vector<void *> allocs;
+    std::vector<LayerPtrs> h_layers;
+    LayerPtrs *d_layers = nullptr;
+    void *lm_head = nullptr, *embed = nullptr;
+    int64_t embed_ld = 0;
+    float *final_norm = nullptr;
+    float *cos_l = nullptr, *sin_l = nullptr, *cos_g = nullptr, *sin_g = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    int64_t kv_layer_stride = 0, kv_row_stride = 0, kv_head_stride = 0;
+    float *h = nullptr, *r = nullptr, *qkv = nullptr, *o_raw = nullptr, *act = nullptr, *mlp_raw = nullptr;
+    float *attn_part = nullptr, *attn_out = nullptr, *logits = nullptr, *emb_acc = nullptr;
+    uint64_t *cand_key = nullptr;
+    int32_t *tok = nullptr, *pos = nullptr, *ids = nullptr, *nvalid = nullptr, *out_tokens = nullptr;
+    int64_t ids_cap = 0, out_cap = 0;
+    double *uniforms = nullptr;
+    uint32_t *sync = nullptr, *err = nullptr;
+    size_t sync_words = 0;
+    std::vector<int32_t> h_pos;
+    int32_t *pinned = nullptr;  // pinned staging for small transfers
+};
+
+template <typename T>
+static mg_status dalloc(mg_model *m, T **p, size_t count, bool zero = true) {
+    void *v = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess)
+        return fail(e == cudaErrorMemoryAllocation ? MG_ERR_OOM : MG_ERR_CUDA, "cudaMalloc(%zu bytes) failed: %s",
+                    bytes, cudaGetErrorString(e));
+    m->allocs.push_back(v);
+    if (zero) {
+        e = cudaMemsetAsync(v, 0, bytes, m->stream);
+        if (e != cudaSuccess) return fail(MG_ERR_CUDA, "cudaMemset failed: %s", cudaGetErrorString(e));
+    }
+    *p = static_cast<T *>(v);
+    return MG_OK;
+}
+
+static int64_t pad128(int64_t x) { return (x + 127) / 128 * 128; }
+static size_t dsize(int dt) { return dt == MG_BF16 || dt == MG_F16 ? 2 : 4; }
+
+// RoPE tables, same float32 formula as the reference (core.mojo:340-348), laid
+// out [position][head_dim / 2].
+static void rope_table(std::vector<float> &c, std::vector<float> &s, int cap, int hd, float base) {
+    const int half = hd / 2;
+    c.assign(static_cast<size_t>(cap) * half, 0.f);
+    s.assign(static_cast<size_t>(cap) * half, 0.f);
+    for (int t = 0; t < cap; ++t)
+        for (int d = 0; d < half; ++d) {
+            const float e = static_cast<float>(d * 2) / static_cast<float>(hd);
+            const float inv_freq = 1.0f / powf(base, e);
+            const float freq = static_cast<float>(t) * inv_freq;
+            c[static_cast<size_t>(t) * half + d] = cosf(freq);
+            s[static_cast<size_t>(t) * half + d] = sinf(freq);
+        }
+}
+
+struct Desc {
+    const void *data = nullptr;
+    std::vector<int64_t> shape;
+    int dtype = MG_F32;
+};
+
+static const Desc *find(const std::map<std::string, Desc> &d, const std::string &name) {
+    auto it = d.find(name);
+    return it == d.end() ? nullptr : &it->second;
+}
+
+// Upload a [rows, cols] host tensor into dst (device, row stride dst_ld,
+// element type m->wdtype or f32), converting and zero-padding columns.
+static mg_status upload_matrix(mg_model *m, const Desc &d, int64_t rows, int64_t cols, void *dst, int dst_dtype,
+                               int64_t dst_ld, void *staging, size_t staging_bytes) {
+    if (d.dtype != MG_F32 && d.dtype != MG_BF16)
+        return fail(MG_ERR_INVALID, "unsupported weight dtype %d (expected F32 or BF16)", d.dtype);
+    const size_t row_bytes = static_cast<size_t>(cols) * dsize(d.dtype);
+    const int64_t rows_per = std::max<int64_t>(1, static_cast<int64_t>(staging_bytes / std::max<size_t>(row_bytes, 1)));
+    for (int64_t r0 = 0; r0 < rows; r0 += rows_per) {
+        const int64_t nr = std::min(rows_per, rows - r0);
+        CU(cudaMemcpyAsync(staging, static_cast<const char *>(d.data) + r0 * row_bytes, nr * row_bytes,
+                           cudaMemcpyHostToDevice, m->stream));
+        CU(convert_rows_launch(staging, d.dtype, nr, cols, static_cast<char *>(dst) + r0 * dst_ld * dsize(dst_dtype),
+                               dst_dtype, dst_ld, m->stream));
+    }
+    return MG_OK;
+}
+
+static mg_status destroy_impl(mg_model *m) {
+    if (!m) return MG_OK;
+    cudaSetDevice(m->dev);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->pinned) cudaFreeHost(m->pinned);
+    if (m->own_stream && m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return MG_OK;
+}
+
+extern "C" mg_status mg_model_destroy(mg_model *m) { return destroy_impl(m); }
+extern "C" void *mg_model_stream(const mg_model *m) { return m ? static_cast<void *>(m->stream) : nullptr; }
+
+static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_options *opt, mg_model *m) {
+    std::map<std::string, Desc> d;
+    for (int i = 0; i < n; ++i) {
+        if (!descs[i].name) return fail(MG_ERR_INVALID, "tensor %d has no name", i);
+        Desc x;
+        x.data = descs[i].data;
+        x.dtype = descs[i].dtype;
+        for (int k = 0; k < descs[i].ndim && k < 4; ++k) x.shape.push_back(descs[i].shape[k]);
+        d[descs[i].name] = x;
+    }
+    m->dev = opt ? opt->device : 0;
+    CU(cudaSetDevice(m->dev));
+    if (opt && opt->stream) {
+        m->stream = static_cast<cudaStream_t>(opt->stream);
+    } else {
+        CU(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+        m->own_stream = true;
+    }
+    m->mode = opt ? opt->mode : 0;
+    m->wdtype = opt ? opt->weight_dtype : MG_F32;
+    if (m->wdtype != MG_F32 && m->wdtype != MG_BF16) return fail(MG_ERR_INVALID, "weight_dtype must be F32 or BF16");
+    m->Bmax = opt && opt->max_batch > 0 ? opt->max_batch : 1;
+    if (m->Bmax > kMaxRows) return fail(MG_ERR_UNSUPPORTED, "max_batch %d exceeds %d", m->Bmax, kMaxRows);
+    m->cap = opt && opt->capacity > 0 ? opt->capacity : 8192;
+    m->seed = opt ? opt->seed : 0;
+    m->decode_path = opt ? opt->decode_path : 0;
+    if (opt && opt->tp_size > 1) return fail(MG_ERR_UNSUPPORTED, "tensor parallelism is not built into this library");
+
+    // ---- dimensions (init_model_mojo, core.mojo:316-325)
+    const Desc *emb = find(d, "model.embed_tokens.weight");
+    const Desc *fnorm = find(d, "model.norm.weight");
+    const Desc *lmh = find(d, "lm_head.weight");
+    if (!emb || !fnorm || !lmh) return fail(MG_ERR_INVALID, "missing embed_tokens, norm or lm_head weights");
+    int L = 0;
+    while (find(d, "model.layers." + std::to_string(L) + ".input_layernorm.weight")) ++L;
+    if (L == 0) return fail(MG_ERR_INVALID, "Invalid standard model weights: no layers found in metadata");
+    auto lw = [&](int l, const char *k) { return find(d, "model.layers." + std::to_string(l) + "." + k); };
+    const Desc *qn0 = lw(0, "self_attn.q_norm.weight");
+    int hd = (qn0 && !qn0->shape.empty() && qn0->shape[0] > 0) ? static_cast<int>(qn0->shape[0]) : 256;
+    const Desc *k0 = lw(0, "self_attn.k_proj.weight");
+    const Desc *q0 = lw(0, "self_attn.q_proj.weight");
+    const Desc *g0 = lw(0, "mlp.gate_proj.weight");
+    if (!k0 || !q0 || !g0 || emb->shape.size() < 2 || lmh->shape.size() < 2)
+        return fail(MG_ERR_INVALID, "missing or malformed projection weights in layer 0");
+    m->L = L;
+    m->hd = hd;
+    m->Hkv = static_cast<int>(k0->shape[0] / hd);
+    m->Hq = static_cast<int>(q0->shape[0] / hd);
+    m->H = static_cast<int>(emb->shape[1]);
+    m->I = static_cast<int>(g0->shape[0]);
+    m->V = static_cast<int>(lmh->shape[0]);
+    if (m->Hkv <= 0 || m->Hq <= 0 || m->Hq % m->Hkv != 0)
+        return fail(MG_ERR_INVALID, "head counts Hq=%d Hkv=%d (head_dim %d) are inconsistent", m->Hq, m->Hkv, hd);
+    if (hd > kMaxHeadDim || hd % 2 != 0) return fail(MG_ERR_UNSUPPORTED, "head_dim %d unsupported", hd);
+    if (m->Hq / m->Hkv > kMaxQPerKv) return fail(MG_ERR_UNSUPPORTED, "more than %d q heads per kv head", kMaxQPerKv);
+    m->A = m->Hq * hd;
+    m->Hp = static_cast<int>(pad128(m->H));
+    m->Ap = static_cast<int>(pad128(m->A));
+    m->Ip = static_cast<int>(pad128(m->I));
+    m->hdp = (hd + 7) / 8 * 8;
+    m->qkv_rows = m->A + 2 * m->Hkv * hd;
+    if (m->mode == 1) {
+        m->window = opt && opt->sliding_window > 0 ? opt->sliding_window : 512;
+        m->global_every = opt && opt->global_every > 0 ? opt->global_every : 6;
+        m->theta_l = opt && opt->rope_theta_local > 0 ? opt->rope_theta_local : 10000.f;
+        m->theta_g = opt && opt->rope_theta_global > 0 ? opt->rope_theta_global : 1000000.f;
+    }
+    // ---- shape checks
+    auto need = [&](const Desc *x, int64_t r, int64_t c, const std::string &nm) -> mg_status {
+        if (!x) return fail(MG_ERR_INVALID, "missing tensor %s", nm.c_str());
+        const int64_t r0 = x->shape.size() > 0 ? x->shape[0] : 0;
+        const int64_t c0 = x->shape.size() > 1 ? x->shape[1] : (c == 0 ? 0 : -1);
+        if (r0 != r || (c != 0 && c0 != c))
+            return fail(MG_ERR_INVALID, "tensor %s has shape (%lld, %lld), expected (%lld, %lld)", nm.c_str(),
+                        (long long)r0, (long long)c0, (long long)r, (long long)c);
+        if (!x->data) return fail(MG_ERR_INVALID, "tensor %s has a null data pointer", nm.c_str());
+        return MG_OK;
+    };
+    TRY(need(emb, m->V, m->H, "model.embed_tokens.weight"));
+    TRY(need(lmh, m->V, m->H, "lm_head.weight"));
+    TRY(need(fnorm, m->H, 0, "model.norm.weight"));
+    for (int l = 0; l < L; ++l) {
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        TRY(need(lw(l, "self_attn.q_proj.weight"), m->A, m->H, p + "self_attn.q_proj.weight"));
+        TRY(need(lw(l, "self_attn.k_proj.weight"), m->Hkv * hd, m->H, p + "self_attn.k_proj.weight"));
+        TRY(need(lw(l, "self_attn.v_proj.weight"), m->Hkv * hd, m->H, p + "self_attn.v_proj.weight"));
+        TRY(need(lw(l, "self_attn.o_proj.weight"), m->H, m->A, p + "self_attn.o_proj.weight"));
+        TRY(need(lw(l, "mlp.gate_proj.weight"), m->I, m->H, p + "mlp.gate_proj.weight"));
+        TRY(need(lw(l, "mlp.up_proj.weight"), m->I, m->H, p + "mlp.up_proj.weight"));
+        TRY(need(lw(l, "mlp.down_proj.weight"), m->H, m->I, p + "mlp.down_proj.weight"));
+        for (const char *k : {"input_layernorm.weight", "post_attention_layernorm.weight",
+                              "pre_feedforward_layernorm.weight", "post_feedforward_layernorm.weight"})
+            TRY(need(lw(l, k), m->H, 0, p + k));
+        const Desc *qn = lw(l, "self_attn.q_norm.weight"), *kn = lw(l, "self_attn.k_norm.weight");
+        if (qn) TRY(need(qn, hd, 0, p + "self_attn.q_norm.weight"));
+        if (kn) TRY(need(kn, hd, 0, p + "self_attn.k_norm.weight"));
+    }
+
+    // ---- launch geometry
+    CU(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->dev));
+    int max_smem = 0;
+    CU(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->dev));
+    const int Kmax = std::max(m->Hp, std::max(m->Ap, m->Ip));
+    const int Gq = m->Hq / m->Hkv;
+    int xs = m->Bmax * Kmax;
+    xs = std::max(xs, Gq * hd + 2 * hd + Gq * kAttTile + 3 * kMaxQPerKv + 8);
+    xs = std::max(xs, static_cast<int>((sizeof(uint32_t) * 264 + sizeof(uint64_t) * 1024 + kMaxTopK * 8 * 2 +
+                                        kMaxTopK * 4) / 4 + 16));
+    m->xs_floats = (xs + 31) / 32 * 32;
+    const size_t static_smem =
+        (m->wdtype == MG_F32 ? decode_static_smem<float>() : decode_static_smem<__nv_bfloat16>()) + 64;
+    m->S = 0;
+    for (int S = 8; S >= 2; --S)
+        if (decode_smem_bytes(S, m->xs_floats) + static_smem <= static_cast<size_t>(max_smem)) {
+            m->S = S;
+            break;
+        }
+    if (m->S < 2)
+        return fail(MG_ERR_UNSUPPORTED, "activation stage of %d floats leaves no room for the weight ring",
+                    m->xs_floats);
+    m->smem = decode_smem_bytes(m->S, m->xs_floats);
+    if (m->wdtype == MG_F32) {
+        CU(decode_prepare<float>(m->smem));
+    } else {
+        CU(decode_prepare<__nv_bfloat16>(m->smem));
+    }
+    const int occ = m->wdtype == MG_F32 ? decode_occupancy<float>(m->smem) : decode_occupancy<__nv_bfloat16>(m->smem);
+    if (occ < 1) return fail(MG_ERR_UNSUPPORTED, "decode kernel does not fit on an SM (smem %zu)", m->smem);
+    m->G = m->num_sms;  // one persistent CTA per SM
+    m->max_ch = (m->cap + kAttTile - 1) / kAttTile;
+
+    // ---- weights
+    const int wd = m->wdtype;
+    const size_t we = dsize(wd);
+    const size_t staging_bytes = 64ull << 20;
+    void *staging = nullptr;
+    TRY(dalloc(m, reinterpret_cast<char **>(&staging), staging_bytes, false));
+    m->h_layers.resize(L);
+    m->weight_bytes = 0;
+    for (int l = 0; l < L; ++l) {
+        LayerPtrs &lp = m->h_layers[l];
+        void *qkv, *o, *gate, *up, *down;
+        TRY(dalloc(m, reinterpret_cast<char **>(&qkv), static_cast<size_t>(m->qkv_rows) * m->Hp * we));
+        TRY(dalloc(m, reinterpret_cast<char **>(&o), static_cast<size_t>(m->H) * m->Ap * we));
+        TRY(dalloc(m, reinterpret_cast<char **>(&gate), static_cast<size_t>(m->I) * m->Hp * we));
+        TRY(dalloc(m, reinterpret_cast<char **>(&up), static_cast<size_t>(m->I) * m->Hp * we));
+        TRY(dalloc(m, reinterpret_cast<char **>(&down), static_cast<size_t>(m->H) * m->Ip * we));
+        const int64_t kvr = static_cast<int64_t>(m->Hkv) * hd;
+        TRY(upload_matrix(m, *lw(l, "self_attn.q_proj.weight"), m->A, m->H, qkv, wd, m->Hp, staging, staging_bytes));
+        TRY(upload_matrix(m, *lw(l, "self_attn.k_proj.weight"), kvr, m->H,
+                          static_cast<char *>(qkv) + static_cast<size_t>(m->A) * m->Hp * we, wd, m->Hp, staging,
+                          staging_bytes));
+        TRY(upload_matrix(m, *lw(l, "self_attn.v_proj.weight"), kvr, m->H,
+                          static_cast<char *>(qkv) + static_cast<size_t>(m->A + kvr) * m->Hp * we, wd, m->Hp,
+                          staging, staging_bytes));
+        TRY(upload_matrix(m, *lw(l, "self_attn.o_proj.weight"), m->H, m->A, o, wd, m->Ap, staging, staging_bytes));
+        TRY(upload_matrix(m, *lw(l, "mlp.gate_proj.weight"), m->I, m->H, gate, wd, m->Hp, staging, staging_bytes));
+        TRY(upload_matrix(m, *lw(l, "mlp.up_proj.weight"), m->I, m->H, up, wd, m->Hp, staging, staging_bytes));
+        TRY(upload_matrix(m, *lw(l, "mlp.down_proj.weight"), m->H, m->I, down, wd, m->Ip, staging, staging_bytes));
+        m->weight_bytes += static_cast<int64_t>(we) * (static_cast<int64_t>(m->qkv_rows) * m->H +
+                                                        static_cast<int64_t>(m->H) * m->A +
+                                                        3 * static_cast<int64_t>(m->I) * m->H);
+        float *norms[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+        const char *nn[4] = {"input_layernorm.weight", "post_attention_layernorm.weight",
+                             "pre_feedforward_layernorm.weight", "post_feedforward_layernorm.weight"};
+        for (int k = 0; k < 4; ++k) {
+            TRY(dalloc(m, &norms[k], m->H));
+            TRY(upload_matrix(m, *lw(l, nn[k]), 1, m->H, norms[k], MG_F32, m->H, staging, staging_bytes));
+        }
+        const Desc *qn = lw(l, "self_attn.q_norm.weight"), *kn = lw(l, "self_attn.k_norm.weight");
+        if (qn) {
+            TRY(dalloc(m, &norms[4], hd));
+            TRY(upload_matrix(m, *qn, 1, hd, norms[4], MG_F32, hd, staging, staging_bytes));
+        }
+        if (kn) {
+            TRY(dalloc(m, &norms[5], hd));
+            TRY(upload_matrix(m, *kn, 1, hd, norms[5], MG_F32, hd, staging, staging_bytes));
+        }
+        lp.qkv = qkv;
+        lp.o = o;
+        lp.gate = gate;
+        lp.up = up;
+        lp.down = down;
+        lp.in_ln = norms[0];
+        lp.post_attn_ln = norms[1];
+        lp.pre_ff_ln = norms[2];
+        lp.post_ff_ln = norms[3];
+        lp.q_norm = norms[4];
+        lp.k_norm = norms[5];
+        lp.is_global = (m->mode == 0) ? 1 : (((l + 1) % m->global_every) == 0 ? 1 : 0);
+    }
+    TRY(dalloc(m, reinterpret_cast<char **>(&m->lm_head), static_cast<size_t>(m->V) * m->Hp * we));
+    TRY(upload_matrix(m, *lmh, m->V, m->H, m->lm_head, wd, m->Hp, staging, staging_bytes));
+    m->weight_bytes += static_cast<int64_t>(we) * m->V * m->H;
+    if (emb->data == lmh->data && emb->dtype == lmh->dtype) {
+        m->embed = m->lm_head;  // tied (convert.py:129-131 writes lm_head as a copy of the embedding)
+    } else {
+        TRY(dalloc(m, reinterpret_cast<char **>(&m->embed), static_cast<size_t>(m->V) * m->Hp * we));
+        TRY(upload_matrix(m, *emb, m->V, m->H, m->embed, wd, m->Hp, staging, staging_bytes));
+    }
+    m->embed_ld = m->Hp;
+    TRY(dalloc(m, &m->final_norm, m->H));
+    TRY(upload_matrix(m, *fnorm, 1, m->H, m->final_norm, MG_F32, m->H, staging, staging_bytes));
+    TRY(dalloc(m, &m->d_layers, L));
+    CU(cudaMemcpyAsync(m->d_layers, m->h_layers.data(), sizeof(LayerPtrs) * L, cudaMemcpyHostToDevice, m->stream));
+
+    // ---- RoPE tables
+    {
+        std::vector<float> c, s;
+        const size_t n_tab = static_cast<size_t>(m->cap) * (hd / 2);
+        TRY(dalloc(m, &m->cos_l, n_tab));
+        TRY(dalloc(m, &m->sin_l, n_tab));
+        rope_table(c, s, m->cap, hd, m->mode == 0 ? 10000.f : m->theta_l);
+        CU(cudaMemcpy(m->cos_l, c.data(), n_tab * 4, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(m->sin_l, s.data(), n_tab * 4, cudaMemcpyHostToDevice));
+        if (m->mode == 0) {
+            m->cos_g = m->cos_l;
+            m->sin_g = m->sin_l;
+        } else {
+            TRY(dalloc(m, &m->cos_g, n_tab));
+            TRY(dalloc(m, &m->sin_g, n_tab));
+            rope_table(c, s, m->cap, hd, m->theta_g);
+            CU(cudaMemcpy(m->cos_g, c.data(), n_tab * 4, cudaMemcpyHostToDevice));
+            CU(cudaMemcpy(m->sin_g, s.data(), n_tab * 4, cudaMemcpyHostToDevice));
+        }
+    }
+    // ---- KV cache [L][Bmax][Hkv][cap][hdp]
+    m->kv_head_stride = static_cast<int64_t>(m->cap) * m->hdp;
+    m->kv_row_stride = m->kv_head_stride * m->Hkv;
+    m->kv_layer_stride = m->kv_row_stride * m->Bmax;
+    TRY(dalloc(m, &m->kc, static_cast<size_t>(m->kv_layer_stride) * L));
+    TRY(dalloc(m, &m->vc, static_cast<size_t>(m->kv_layer_stride) * L));
+    // ---- activations
+    const int B = m->Bmax;
+    TRY(dalloc(m, &m->h, static_cast<size_t>(B) * m->H));
+    TRY(dalloc(m, &m->r, static_cast<size_t>(B) * m->H));
+    TRY(dalloc(m, &m->qkv, static_cast<size_t>(B) * m->qkv_rows));
+    TRY(dalloc(m, &m->o_raw, static_cast<size_t>(B) * m->H));
+    TRY(dalloc(m, &m->act, static_cast<size_t>(B) * m->Ip));
+    TRY(dalloc(m, &m->mlp_raw, static_cast<size_t>(B) * m->H));
+    TRY(dalloc(m, &m->attn_part, static_cast<size_t>(B) * m->Hkv * m->max_ch * Gq * (hd + 2)));
+    TRY(dalloc(m, &m->attn_out, static_cast<size_t>(B) * m->Ap));
+    TRY(dalloc(m, &m->logits, static_cast<size_t>(B) * m->V));
+    TRY(dalloc(m, &m->emb_acc, static_cast<size_t>(B) * m->H));
+    TRY(dalloc(m, &m->cand_key, static_cast<size_t>(B) * m->G * kMaxTopK));
+    TRY(dalloc(m, &m->tok, kMaxRows));
+    TRY(dalloc(m, &m->pos, kMaxRows));
+    TRY(dalloc(m, &m->uniforms, kMaxRows));
+    m->sync_words = num_phases(L) + L + kMaxRows * m->Hkv + 1;
+    TRY(dalloc(m, &m->sync, m->sync_words));
+    TRY(dalloc(m, &m->err, 1));
+    CU(cudaMallocHost(&m->pinned, 4096));
+    m->h_pos.assign(kMaxRows, 0);
+    CU(cudaStreamSynchronize(m->stream));
+    cudaFree(staging);
+    m->allocs.erase(std::find(m->allocs.begin(), m->allocs.end(), staging));
+    return MG_OK;
+}
+
+extern "C" mg_status mg_model_create(const mg_tensor_desc *descs, int32_t n, const mg_options *opt, mg_model **out) {
+    if (!out) return fail(MG_ERR_INVALID, "out is null");
+    *out = nullptr;
+    if (!descs || n <= 0) return fail(MG_ERR_INVALID, "no tensors given");
+    mg_model *m = new mg_model();
+    mg_status st = create_impl(descs, n, opt, m);
+    if (st != MG_OK) {
+        std::string keep = g_err;
+        destroy_impl(m);
+        g_err = keep;
+        return st;
+    }
+    *out = m;
+    return MG_OK;
+}
+
+extern "C" mg_status mg_model_info_get(const mg_model *m, mg_model_info *info) {
+    if (!m || !info) return fail(MG_ERR_INVALID, "null argument");
+    info->num_layers = m->L;
+    info->num_heads = m->Hq;
+    info->num_kv_heads = m->Hkv;
+    info->head_dim = m->hd;
+    info->hidden_size = m->H;
+    info->intermediate_size = m->I;
+    info->vocab_size = m->V;
+    info->max_seq_len = m->cap;
+    info->max_batch = m->Bmax;
+    info->mode = m->mode;
+    info->weight_dtype = m->wdtype;
+    info->tp_size = 1;
+    info->weight_bytes_per_step = m->weight_bytes;
+    info->kv_bytes_per_pos = static_cast<int64_t>(2) * m->L * m->Hkv * m->hd * 4;
+    info->num_sms = m->num_sms;
+    info->persistent_ctas = m->G;
+    return MG_OK;
+}
+
+// ---------------------------------------------------------------- launches
+static DecodeParams base_params(mg_model *m, int B) {
+    DecodeParams p;
+    memset(&p, 0, sizeof p);
+    p.L = m->L;
+    p.H = m->H;
+    p.Hp = m->Hp;
+    p.Hq = m->Hq;
+    p.Hkv = m->Hkv;
+    p.hd = m->hd;
+    p.hdp = m->hdp;
+    p.I = m->I;
+    p.Ip = m->Ip;
+    p.V = m->V;
+    p.A = m->A;
+    p.Ap = m->Ap;
+    p.qkv_rows = m->qkv_rows;
+    p.B = B;
+    p.cap = m->cap;
+    p.window = m->window;
+    p.S = m->S;
+    p.max_ch = m->max_ch;
+    p.xs_floats = m->xs_floats;
+    p.layers = m->d_layers;
+    p.lm_head = m->lm_head;
+    p.embed = m->embed;
+    p.embed_ld = m->embed_ld;
+    p.final_norm = m->final_norm;
+    p.rope_cos_l = m->cos_l;
+    p.rope_sin_l = m->sin_l;
+    p.rope_cos_g = m->cos_g;
+    p.rope_sin_g = m->sin_g;
+    p.kc = m->kc;
+    p.vc = m->vc;
+    p.kv_layer_stride = m->kv_layer_stride;
+    p.kv_row_stride = m->kv_row_stride;
+    p.kv_head_stride = m->kv_head_stride;
+    p.h = m->h;
+    p.r = m->r;
+    p.qkv = m->qkv;
+    p.o_raw = m->o_raw;
+    p.act = m->act;
+    p.mlp_raw = m->mlp_raw;
+    p.attn_part = m->attn_part;
+    p.attn_out = m->attn_out;
+    p.logits = m->logits;
+    p.cand_key = m->cand_key;
+    p.emb_acc = m->emb_acc;
+    p.tok = m->tok;
+    p.pos = m->pos;
+    p.seed = m->seed;
+    p.sync = m->sync;
+    p.err = m->err;
+    p.n_phases = num_phases(m->L);
+    p.ph_begin = 0;
+    p.ph_end = p.n_phases;
+    return p;
+}
+
+// Chunk size for split-KV attention: about `target` chunks per (row, kv head).
+static int att_chunk(const mg_model *m, int B, int max_ctx) {
+    const int target = std::max(1, std::min(32, m->G / std::max(1, B * m->Hkv)));
+    int ch = (max_ctx + target - 1) / target;
+    ch = (ch + kAttTile - 1) / kAttTile * kAttTile;
+    ch = std::max(ch, kAttTile);
+    const int min_ch = (m->cap + m->max_ch - 1) / m->max_ch;
+    return std::max(ch, (min_ch + kAttTile - 1) / kAttTile * kAttTile);
+}
+
+static mg_status run_decode(mg_model *m, DecodeParams &p, int max_ctx) {
+    p.att_ch = att_chunk(m, p.B, max_ctx);
+    const bool persistent = m->decode_path == 0;
+    if (persistent) {
+        cudaError_t e = m->wdtype == MG_F32 ? decode_launch<float>(p, m->G, m->smem, m->stream, true)
+                                            : decode_launch<__nv_bfloat16>(p, m->G, m->smem, m->stream, true);
+        if (e != cudaSuccess) return fail(MG_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
+    } else {
+        for (int ph = 0; ph < p.n_phases; ++ph) {
+            DecodeParams q = p;
+            q.ph_begin = ph;
+            q.ph_end = ph + 1;
+            cudaError_t e = m->wdtype == MG_F32 ? decode_launch<float>(q, m->G, m->smem, m->stream, false)
+                                                : decode_launch<__nv_bfloat16>(q, m->G, m->smem, m->stream, false);
+            if (e != cudaSuccess) return fail(MG_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
+        }
+    }
+    return MG_OK;
+}
+
+// Reads and clears the device error word (synchronises the stream).
+static mg_status check_device(mg_model *m) {
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return fail(MG_ERR_CUDA, "device error: %s", cudaGetErrorString(e));
+    uint32_t code = 0;
+    CU(cudaMemcpy(&code, m->err, 4, cudaMemcpyDeviceToHost));
+    if (code != 0) {
+        CU(cudaMemset(m->err, 0, 4));
+        CU(cudaMemset(m->sync, 0, m->sync_words * 4));
+        const uint32_t kind = code & 0xffff0000u;
+        if (kind == kErrBadToken) return fail(MG_ERR_INVALID, "token id out of range in row %u", code & 0xffffu);
+        if (kind == kErrBadPos) return fail(MG_ERR_SEQ_EXCEEDED, "Sequence length exceeded");
+        return fail(MG_ERR_TIMEOUT, "decode kernel gave up waiting (code 0x%08x); results discarded", code);
+    }
+    return MG_OK;
+}
+
+struct SampleCfg {
+    int topk = 0;      // fused candidates
+    bool fused = false;
+    bool general = false;
+};
+
+static SampleCfg sample_cfg(const mg_model *m, const mg_sampling *s) {
+    SampleCfg c;
+    if (!s) return c;
+    if (s->temperature <= 0.0) {
+        c.topk = 1;
+        c.fused = true;
+    } else if (s->top_k > 0 && s->top_k < m->V && s->top_k <= kMaxTopK) {
+        c.topk = s->top_k;
+        c.fused = true;
+    } else if (m->V <= kMaxTopK) {
+        c.topk = m->V;
+        c.fused = true;
+    } else {
+        c.general = true;
+    }
+    return c;
+}
+
+static mg_status validate_rows(mg_model *m, int batch) {
+    if (batch <= 0 || batch > m->Bmax) return fail(MG_ERR_INVALID, "batch %d outside [1, %d]", batch, m->Bmax);
+    return MG_OK;
+}
+
+static mg_status step_impl(mg_model *m, int batch, float *logits_host, int32_t *sampled_host, const mg_sampling *s,
+                           bool check) {
+    for (int b = 0; b < batch; ++b)
+        if (m->h_pos[b] >= m->cap) return fail(MG_ERR_SEQ_EXCEEDED, "Sequence length exceeded");
+    const SampleCfg sc = sample_cfg(m, s);
+    DecodeParams p = base_params(m, batch);
+    const bool need_logits = logits_host != nullptr || sc.general || sc.fused;
+    p.lm_mode = need_logits ? kLmLogits : kLmNone;
+    p.topk = sc.fused ? sc.topk : 0;
+    p.sample = sc.fused ? 1 : 0;
+    if (s) {
+        p.temperature = s->temperature;
+        p.top_p = s->top_p;
+        p.top_k_req = s->top_k;
+        if (s->uniforms_host) {
+            CU(cudaMemcpyAsync(m->uniforms, s->uniforms_host, sizeof(double) * batch, cudaMemcpyHostToDevice,
+                               m->stream));
+            p.uniforms = m->uniforms;
+        }
+    }
+    p.rng_offset = m->rng_offset;
+    p.out_tokens = nullptr;
+    int max_ctx = 0;
+    for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, m->h_pos[b] + 1);
+    TRY(run_decode(m, p, max_ctx));
+    if (sc.general) {
+        CU(sample_rows_launch(m->logits, m->V, batch, m->V, s->temperature, s->top_k, s->top_p, p.uniforms, m->seed,
+                              m->rng_offset, nullptr, m->tok, m->stream));
+    }
+    if (s) m->rng_offset += 1;
+    for (int b = 0; b < batch; ++b) m->h_pos[b] += 1;
+    if (logits_host)
+        CU(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * batch * m->V, cudaMemcpyDeviceToHost, m->stream));
+    if (sampled_host && s) {
+        CU(cudaMemcpyAsync(m->pinned, m->tok, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, m->stream));
+    }
+    if (check || logits_host || sampled_host) {
+        mg_status st = check_device(m);
+        if (st != MG_OK) {
+            for (int b = 0; b < batch; ++b) m->h_pos[b] -= 1;
+            CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+            return st;
+        }
+        if (sampled_host && s) memcpy(sampled_host, m->pinned, sizeof(int32_t) * batch);
+    }
+    return MG_OK;
+}
+
+extern "C" mg_status mg_step(mg_model *m, const int32_t *token_ids_host, int32_t batch, float *logits_host,
+                             int32_t *sampled_host, const mg_sampling *s) {
+    if (!m || !token_ids_host) return fail(MG_ERR_INVALID, "null argument");
+    TRY(validate_rows(m, batch));
+    CU(cudaSetDevice(m->dev));
+    for (int b = 0; b < batch; ++b)
+        if (token_ids_host[b] < 0 || token_ids_host[b] >= m->V)
+            return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", token_ids_host[b], m->V);
+    memcpy(m->pinned, token_ids_host, sizeof(int32_t) * batch);
+    CU(cudaMemcpyAsync(m->tok, m->pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, m->stream));
+    return step_impl(m, batch, logits_host, sampled_host, s, true);
+}
+
+extern "C" mg_status mg_set_tokens(mg_model *m, const int32_t *token_ids_host, int32_t batch) {
+    if (!m || !token_ids_host) return fail(MG_ERR_INVALID, "null argument");
+    TRY(validate_rows(m, batch));
+    CU(cudaSetDevice(m->dev));
+    for (int b = 0; b < batch; ++b)
+        if (token_ids_host[b] < 0 || token_ids_host[b] >= m->V)
+            return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", token_ids_host[b], m->V);
+    CU(cudaMemcpyAsync(m->tok, token_ids_host, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    return MG_OK;
+}
+
+extern "C" mg_status mg_generate(mg_model *m, int32_t n_steps, int32_t batch, const mg_sampling *s,
+                                 int32_t *tokens_host) {
+    if (!m || !s) return fail(MG_ERR_INVALID, "null argument");
+    TRY(validate_rows(m, batch));
+    if (n_steps <= 0) return MG_OK;
+    CU(cudaSetDevice(m->dev));
+    for (int b = 0; b < batch; ++b)
+        if (m->h_pos[b] + n_steps > m->cap) return fail(MG_ERR_SEQ_EXCEEDED, "Sequence length exceeded");
+    const int64_t need = static_cast<int64_t>(n_steps) * batch;
+    if (need > m->out_cap) {
+        int32_t *buf = nullptr;
+        TRY(dalloc(m, &buf, need));
+        m->out_tokens = buf;
+        m->out_cap = need;
+    }
+    const SampleCfg sc = sample_cfg(m, s);
+    const std::vector<int32_t> pos0 = m->h_pos;
+    for (int t = 0; t < n_steps; ++t) {
+        DecodeParams p = base_params(m, batch);
+        p.lm_mode = kLmLogits;
+        p.topk = sc.fused ? sc.topk : 0;
+        p.sample = sc.fused ? 1 : 0;
+        p.temperature = s->temperature;
+        p.top_p = s->top_p;
+        p.top_k_req = s->top_k;
+        p.rng_offset = m->rng_offset;
+        p.out_tokens = m->out_tokens + static_cast<int64_t>(t) * batch;
+        int max_ctx = 0;
+        for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, m->h_pos[b] + 1);
+        TRY(run_decode(m, p, max_ctx));
+        if (sc.general)
+            CU(sample_rows_launch(m->logits, m->V, batch, m->V, s->temperature, s->top_k, s->top_p, nullptr, m->seed,
+                                  m->rng_offset, p.out_tokens, m->tok, m->stream));
+        m->rng_offset += 1;
+        for (int b = 0; b < batch; ++b) m->h_pos[b] += 1;
+    }
+    if (tokens_host)
+        CU(cudaMemcpyAsync(tokens_host, m->out_tokens, sizeof(int32_t) * need, cudaMemcpyDeviceToHost, m->stream));
+    mg_status st = check_device(m);
+    if (st != MG_OK) {
+        m->h_pos = pos0;
+        CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+    }
+    return st;
+}
+
+static mg_status upload_ids(mg_model *m, const int32_t *ids, const int32_t *lens, int batch, int max_len) {
+    const int64_t need = static_cast<int64_t>(batch) * max_len;
+    if (need > m->ids_cap) {
+        int32_t *buf = nullptr;
+        TRY(dalloc(m, &buf, need));
+        m->ids = buf;
+        m->ids_cap = need;
+    }
+    if (!m->nvalid) TRY(dalloc(m, &m->nvalid, kMaxRows));
+    for (int b = 0; b < batch; ++b) {
+        if (lens[b] < 0 || lens[b] > max_len) return fail(MG_ERR_INVALID, "row %d length %d outside [0, %d]", b, lens[b], max_len);
+        for (int t = 0; t < lens[b]; ++t) {
+            const int32_t id = ids[static_cast<int64_t>(b) * max_len + t];
+            if (id < 0 || id >= m->V) return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", id, m->V);
+        }
+    }
+    CU(cudaMemcpyAsync(m->ids, ids, sizeof(int32_t) * need, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(m->nvalid, lens, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, m->stream));
+    return MG_OK;
+}
+
+extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
+                                int32_t max_len) {
+    if (!m || !token_ids_host || !lens_host) return fail(MG_ERR_INVALID, "null argument");
+    TRY(validate_rows(m, batch));
+    CU(cudaSetDevice(m->dev));
+    int longest = 0;
+    for (int b = 0; b < batch; ++b) {
+        longest = std::max(longest, lens_host[b]);
+        if (m->h_pos[b] + lens_host[b] > m->cap) return fail(MG_ERR_SEQ_EXCEEDED, "Sequence length exceeded");
+    }
+    if (longest == 0) return MG_OK;
+    TRY(upload_ids(m, token_ids_host, lens_host, batch, max_len));
+    std::vector<int32_t> pos0 = m->h_pos;
+    for (int t = 0; t < longest; ++t) {
+        DecodeParams p = base_params(m, batch);
+        p.lm_mode = kLmNone;
+        p.ids = m->ids;
+        p.ids_ld = max_len;
+        p.nvalid = m->nvalid;
+        p.step_t = t;
+        int max_ctx = 0;
+        for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, pos0[b] + std::min(t, lens_host[b]) + 1);
+        TRY(run_decode(m, p, max_ctx));
+    }
+    // the last fed token becomes the current token of each row
+    for (int b = 0; b < batch; ++b) m->h_pos[b] = pos0[b] + lens_host[b];
+    mg_status st = check_device(m);
+    if (st != MG_OK) {
+        m->h_pos = pos0;
+        CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+    }
+    return st;
+}
+
+extern "C" mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
+                              int32_t max_len, float *out_host) {
+    if (!m || !token_ids_host || !lens_host || !out_host) return fail(MG_ERR_INVALID, "null argument");
+    if (batch <= 0) return fail(MG_ERR_INVALID, "inputs must contain at least one row");
+    CU(cudaSetDevice(m->dev));
+    for (int b = 0; b < batch; ++b) {
+        if (lens_host[b] <= 0) return fail(MG_ERR_INVALID, "inputs must contain at least one token");
+        if (lens_host[b] > m->cap) return fail(MG_ERR_SEQ_EXCEEDED, "Sequence length exceeded");
+    }
+    const std::vector<int32_t> pos_saved = m->h_pos;
+    std::vector<float> acc(static_cast<size_t>(m->Bmax) * m->H);
+    for (int b0 = 0; b0 < batch; b0 += m->Bmax) {
+        const int nb = std::min(m->Bmax, batch - b0);
+        int longest = 0;
+        for (int b = 0; b < nb; ++b) longest = std::max(longest, lens_host[b0 + b]);
+        TRY(upload_ids(m, token_ids_host + static_cast<int64_t>(b0) * max_len, lens_host + b0, nb, max_len));
+        CU(cudaMemsetAsync(m->pos, 0, sizeof(int32_t) * kMaxRows, m->stream));
+        CU(cudaMemsetAsync(m->emb_acc, 0, sizeof(float) * m->Bmax * m->H, m->stream));
+        for (int t = 0; t < longest; ++t) {
+            DecodeParams p = base_params(m, nb);
+            p.lm_mode = kLmEmbed;
+            p.ids = m->ids;
+            p.ids_ld = max_len;
+            p.nvalid = m->nvalid;
+            p.step_t = t;
+            TRY(run_decode(m, p, t + 1));
+        }
+        CU(cudaMemcpyAsync(acc.data(), m->emb_acc, sizeof(float) * nb * m->H, cudaMemcpyDeviceToHost, m->stream));
+        TRY(check_device(m));
+        for (int b = 0; b < nb; ++b) {
+            const float scale = 1.0f / static_cast<float>(lens_host[b0 + b]);  // layers.mojo:368-370
+            for (int i = 0; i < m->H; ++i)
+                out_host[static_cast<int64_t>(b0 + b) * m->H + i] = acc[static_cast<size_t>(b) * m->H + i] * scale;
+        }
+    }
+    m->h_pos = pos_saved;
+    CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+    return MG_OK;
+}
+
+extern "C" mg_status mg_set_pos(mg_model *m, int32_t row, int32_t pos) {
+    if (!m) return fail(MG_ERR_INVALID, "null model");
+    if (row >= m->Bmax || row < -1) return fail(MG_ERR_INVALID, "row %d outside [-1, %d)", row, m->Bmax);
+    if (pos < 0 || pos > m->cap) return fail(MG_ERR_INVALID, "pos %d outside [0, %d]", pos, m->cap);
+    CU(cudaSetDevice(m->dev));
+    for (int b = 0; b < kMaxRows; ++b)
+        if (row == -1 || row == b) m->h_pos[b] = pos;
+    CU(cudaMemcpyAsync(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    return MG_OK;
+}
+
+extern "C" mg_status mg_get_pos(const mg_model *m, int32_t *pos_host, int32_t n) {
+    if (!m || !pos_host) return fail(MG_ERR_INVALID, "null argument");
+    for (int i = 0; i < n && i < kMaxRows; ++i) pos_host[i] = m->h_pos[i];
+    return MG_OK;
+}
+
+extern "C" mg_status mg_read_kv(const mg_model *m, int32_t layer, int32_t row, int32_t pos, float *k_host,
+                                float *v_host) {
+    if (!m || !k_host || !v_host) return fail(MG_ERR_INVALID, "null argument");
+    if (layer < 0 || layer >= m->L || row < 0 || row >= m->Bmax || pos < 0 || pos >= m->cap)
+        return fail(MG_ERR_INVALID, "layer/row/pos out of range");
+    CU(cudaSetDevice(m->dev));
+    CU(cudaStreamSynchronize(m->stream));
+    for (int h = 0; h < m->Hkv; ++h) {
+        const size_t off = static_cast<size_t>(layer) * m->kv_layer_stride + static_cast<size_t>(row) * m->kv_row_stride +
+                           static_cast<size_t>(h) * m->kv_head_stride + static_cast<size_t>(pos) * m->hdp;
+        CU(cudaMemcpy(k_host + static_cast<size_t>(h) * m->hd, m->kc + off, sizeof(float) * m->hd,
+                      cudaMemcpyDeviceToHost));
+        CU(cudaMemcpy(v_host + static_cast<size_t>(h) * m->hd, m->vc + off, sizeof(float) * m->hd,
+                      cudaMemcpyDeviceToHost));
+    }
+    return MG_OK;
+}
+
+extern "C" mg_status mg_sample(const float *logits_host, int32_t batch, int32_t vocab, const mg_sampling *s,
+                               uint64_t seed, uint64_t offset, int32_t *out_host) {
+    if (!logits_host || !s || !out_host || batch <= 0 || vocab <= 0) return fail(MG_ERR_INVALID, "bad argument");
+    float *dl = nullptr;
+    int32_t *dout = nullptr;
+    double *du = nullptr;
+    const size_t lb = sizeof(float) * static_cast<size_t>(batch) * vocab;
+    CU(cudaMalloc(&dl, lb));
+    cudaError_t e = cudaMalloc(&dout, sizeof(int32_t) * batch);
+    if (e == cudaSuccess && s->uniforms_host) e = cudaMalloc(&du, sizeof(double) * batch);
+    if (e == cudaSuccess) e = cudaMemcpy(dl, logits_host, lb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && du) e = cudaMemcpy(du, s->uniforms_host, sizeof(double) * batch, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = sample_rows_launch(dl, vocab, batch, vocab, s->temperature, s->top_k, s->top_p, du, seed, offset, dout,
+                               nullptr, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(out_host, dout, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost);
+    cudaFree(dl);
+    cudaFree(dout);
+    if (du) cudaFree(du);
+    if (e != cudaSuccess) return fail(MG_ERR_CUDA, "mg_sample: %s", cudaGetErrorString(e));
+    return MG_OK;
+}
+
+extern "C" mg_status mg_nccl_unique_id(void *out128) {
+    (void)out128;
+    return fail(MG_ERR_UNSUPPORTED, "tensor parallelism is not built into this library");
+}
