@@ -1,0 +1,320 @@
+"""Benchmark: batch-1 decode tokens/s of Gemma3-1B and achieved HBM GB/s.
+
+Workload (one "step"): with a 512-token random prompt already in the KV
+cache, decode 256 tokens at batch 1 with temperature 0.7 / top-k 64, each
+drawn on the device and fed back (positions 512..767).  Weights are seeded
+random-init (N(0, 0.02)) in the reference dtype (fp32); no checkpoint or
+dataset is reachable offline, so the data is synthetic.
+
+value: decode tokens/s with everything resident in HBM (CUDA events on the
+model's stream around K steps, max over ranks).  e2e: the same decode through
+the C ABI call a plugin makes per token (mg_step with a host token id in and
+the sampled host id out).  roofline: algorithmic bytes of one decode-kernel
+launch (weights + KV read/write + logits write) / its average duration,
+against the measured HBM copy bandwidth.  cpu_baseline: the oracle (C port of
+the reference engine, 1 thread like the reference) on a bounded sample.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIG = "gemma3-1b"
+PROMPT = 512
+DECODE = 256
+TEMPERATURE, TOP_K, TOP_P = 0.7, 64, 1.0
+METRIC = "batch-1 decode tokens/s (Gemma3-1B) and achieved HBM GB/s vs 8 TB/s peak"
+UNIT = "tokens/s"
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int) -> None:
+        self.gpu = gpu
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+
+    def __enter__(self) -> ClockSampler:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self) -> dict:
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def algorithmic_bytes(info, pos0: int, n: int) -> float:
+    """Average bytes one decode-kernel launch must move for positions pos0..pos0+n-1."""
+    kv_row = 2 * info.num_kv_heads * info.head_dim * 4  # K+V fp32, one layer, one position
+    ctx_avg = pos0 + (n + 1) / 2.0
+    kv_read = info.num_layers * kv_row * ctx_avg
+    kv_write = info.num_layers * kv_row
+    logits = info.vocab_size * 4
+    emb_row = info.hidden_size * (4 if info.weight_dtype == 0 else 2)
+    return float(info.weight_bytes_per_step + kv_read + kv_write + logits + emb_row)
+
+
+def cpu_baseline(weights: dict, threads: int, n_tokens: int) -> dict:
+    """Oracle port on the host: n_tokens decode steps from an empty cache."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle  # noqa: PLC0415
+
+    oracle.set_threads(threads)
+    ref = oracle.RefModel(weights, max_seq_len=PROMPT + DECODE)
+    toks = [int(t) for t in np.random.default_rng(1).integers(0, 262144, n_tokens)]
+    ref.step(toks[0])  # warm the caches
+    t0 = time.perf_counter()
+    for t in toks[1:]:
+        ref.step(t)
+    dt = time.perf_counter() - t0
+    oracle.set_threads(1)
+    ref.close()
+    return {"value": (n_tokens - 1) / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n_tokens - 1} Gemma3-1B decode steps (fp32, full 262144-vocab lm_head) from an empty cache "
+                      f"on {threads} host thread(s); attention is <2% of bytes per token at pos<=768"}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime  # noqa: PLC0415
+
+        import torch  # noqa: PLC0415
+        import torch.distributed as dist  # noqa: PLC0415
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def dist_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch  # noqa: PLC0415
+    import torch.distributed as dist  # noqa: PLC0415
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        dist.barrier()
+
+
+def run_reference(args, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    from mogemma_b200 import synth  # noqa: PLC0415
+
+    threads = len(os.sched_getaffinity(0))
+    d = synth.CONFIGS[CONFIG]
+    w = synth.make_weights(d, seed=0)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle  # noqa: PLC0415
+
+    oracle.set_threads(threads)
+    ref = oracle.RefModel(w, max_seq_len=PROMPT + DECODE)
+    per_step = 4
+    rng = np.random.default_rng(1)
+    for _ in range(args.warmup):
+        for t in rng.integers(0, d.vocab, per_step):
+            ref.step(int(t))
+    ref.pos = 0
+    t0 = time.perf_counter()
+    n = 0
+    for _ in range(args.steps):
+        for t in rng.integers(0, d.vocab, per_step):
+            ref.step(int(t))
+            n += 1
+    dt = time.perf_counter() - t0
+    v = n / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, uniform random ids)",
+        "config": {"workload": "Gemma3-1B batch-1 decode (fp32 weights)", "global_batch": 1, "seq_len": PROMPT + DECODE,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{per_step} decode steps per step on {threads} threads (OpenMP over output rows; "
+                                   "per-row arithmetic identical to the single-threaded reference engine)"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--weight-dtype", default="f32", choices=["f32", "bf16"])
+    ap.add_argument("--cpu-sample", type=int, default=25)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import ctypes  # noqa: PLC0415
+
+    import torch  # noqa: PLC0415
+
+    from mogemma_b200 import _core, synth  # noqa: PLC0415
+
+    d = synth.CONFIGS[CONFIG]
+    weights = synth.make_weights(d, seed=0, bf16=args.weight_dtype == "bf16")
+    llm = _core.init_model(synth.metadata_of(weights), device=local, capacity=PROMPT + DECODE, max_batch=1,
+                           weight_dtype=args.weight_dtype, seed=1234 + rank)
+    h = llm["_handle"]
+    info = h.info
+    lib = _core.lib()
+    prompt = [int(t) for t in synth.prompt_ids(PROMPT, d.vocab, seed=1)]
+    _core.prefill(llm, prompt[:-1])
+    s, _keep = _core._sampling(TEMPERATURE, TOP_K, TOP_P)
+    first = np.array([prompt[-1]], np.int32)
+    stream = torch.cuda.ExternalStream(h.stream, device=torch.device("cuda", local))
+
+    def device_step() -> None:
+        # positions 511.. : feed the last prompt token, then 255 sampled tokens
+        _core._check(lib.mg_set_pos(h.ptr, 0, PROMPT - 1))
+        _core._check(lib.mg_set_tokens(h.ptr, first.ctypes.data_as(_core._I32P), 1))
+        _core._check(lib.mg_generate(h.ptr, DECODE, 1, ctypes.byref(s), None))
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            device_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = ev0.elapsed_time(ev1)
+    ms = dist_max(ms, world)
+    tokens = args.steps * DECODE * world
+    value = tokens / (ms / 1000.0)
+    ms_launch = ms / (args.steps * DECODE)
+    bytes_launch = algorithmic_bytes(info, PROMPT - 1, DECODE)
+    achieved = bytes_launch / (ms_launch / 1000.0) / 1e9
+    pk = peaks()
+
+    # e2e: per-token C-ABI call with host buffers (token id in, sampled id out)
+    ids = np.zeros(1, np.int32)
+    out = np.zeros(1, np.int32)
+    idp, outp = ids.ctypes.data_as(_core._I32P), out.ctypes.data_as(_core._I32P)
+
+    def e2e_step() -> None:
+        _core._check(lib.mg_set_pos(h.ptr, 0, PROMPT - 1))
+        ids[0] = prompt[-1]
+        for _ in range(DECODE):
+            _core._check(lib.mg_step(h.ptr, idp, 1, None, outp, ctypes.byref(s)))
+            ids[0] = out[0]
+
+    e2e_step()
+    barrier(world)
+    t0 = time.perf_counter()
+    e2e_steps = max(1, min(args.steps, 3))
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = dist_max(time.perf_counter() - t0, world)
+    e2e_value = e2e_steps * DECODE * world / e2e_s
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(weights, 1, args.cpu_sample)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.weight_dtype,
+            "data": "synthetic (seeded N(0,0.02) random-init weights, uniform random prompt ids)",
+            "config": {"workload": f"Gemma3-1B batch-1 decode: {PROMPT}-token prompt then {DECODE} tokens "
+                                   f"(T={TEMPERATURE}, top-k {TOP_K}), {args.weight_dtype} weights",
+                       "model": CONFIG, "global_batch": world, "seq_len": PROMPT + DECODE,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": f"inputs larger than L2 ({info.weight_bytes_per_step / 1e9:.2f} GB of weights per token)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * DECODE,
+                    "d2h_bytes_per_step": 4 * DECODE},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                         "peak_source": pk["source"], "kernel": "decode_kernel (one launch per token)",
+                         "algorithmic_bytes_per_launch": bytes_launch},
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps * DECODE,
+            "ms_per_token": ms_launch,
+        }
+        print(json.dumps(line), flush=True)
+    h.close()
+    if world > 1:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

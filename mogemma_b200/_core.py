@@ -127,9 +127,11 @@ _lib.mg_sample.argtypes = [_F32P, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER
 _lib.mg_embed.argtypes = [_P, _I32P, _I32P, ctypes.c_int32, ctypes.c_int32, _F32P]
 _lib.mg_read_kv.argtypes = [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _F32P, _F32P]
 _lib.mg_nccl_unique_id.argtypes = [_P]
+_lib.mg_trace_enable.argtypes = [_P, ctypes.c_int32]
+_lib.mg_trace_read.argtypes = [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)]
 for _f in ("mg_model_create", "mg_model_info_get", "mg_model_destroy", "mg_set_pos", "mg_get_pos", "mg_step",
            "mg_prefill", "mg_generate", "mg_set_tokens", "mg_sample", "mg_embed", "mg_read_kv",
-           "mg_nccl_unique_id"):
+           "mg_nccl_unique_id", "mg_trace_enable", "mg_trace_read"):
     getattr(_lib, _f).restype = ctypes.c_int
 
 
@@ -185,6 +187,26 @@ class ModelHandle:
         _check(_lib.mg_set_pos(self.ptr, row, int(pos)))
         if row in (-1, 0):
             self.pos = int(pos)
+
+    def trace(self, on: bool = True) -> None:
+        """Record a per-CTA, per-phase timeline of every decode launch."""
+        _check(_lib.mg_trace_enable(self.ptr, int(on)))
+
+    def read_trace(self) -> tuple[npt.NDArray[np.uint64], npt.NDArray[np.uint64]]:
+        """Timeline of the last launch: ([ctas, phases, slots] stamps, [ctas, 2] kernel begin/end) in ns.
+
+        Slots: start, ready, first tile, end, producer start, producer end,
+        then for attention phases: q/k/v loaded, normed+roped, tiles done, partial written.
+        """
+        n = ctypes.c_int64(0)
+        _check(_lib.mg_trace_read(self.ptr, (ctypes.c_uint64 * 1)(), 0, ctypes.byref(n)))
+        buf = np.zeros(int(n.value), np.uint64)
+        _check(_lib.mg_trace_read(self.ptr, buf.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), buf.size,
+                                  ctypes.byref(n)))
+        g = int(self.info.persistent_ctas)
+        nph = 5 * int(self.info.num_layers) + 2
+        slots = (buf.size - 2 * g) // (g * nph)
+        return buf[: g * nph * slots].reshape(g, nph, slots), buf[g * nph * slots:].reshape(g, 2)
 
     def get_pos(self) -> list[int]:
         out = np.zeros(8, np.int32)

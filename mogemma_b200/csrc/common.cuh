@@ -48,6 +48,7 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
 __device__ __forceinline__ void red_release_add_u32(uint32_t *p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void set_error(uint32_t *err, uint32_t code) { atomicCAS(err, 0u, code); }
 
 // Wait until *ctr >= target (acquire).  Returns false on error/timeout.
@@ -94,16 +95,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0u;
 }
-// Bounded wait for the phase with `parity` to complete.
+// Non-blocking probe of a phase.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0u;
+}
+// Bounded wait for the phase with `parity` to complete.  The error word and
+// the clock are consulted only every 32 polls, keeping the hot poll local.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (true) {
+    for (uint32_t n = 1;; ++n) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (ld_relaxed_u32(err) != 0u) return false;
-        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
-            set_error(err, code);
-            return false;
+        if ((n & 31u) == 0u) {
+            if (ld_relaxed_u32(err) != 0u) return false;
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+                set_error(err, code);
+                return false;
+            }
         }
     }
 }
@@ -125,6 +141,10 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "%4;" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+// Prefetch [src, src + bytes) into L2 (no completion tracking).  16-byte aligned, multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;

@@ -22,6 +22,7 @@ constexpr int kMaxHeadDim = 256;
 constexpr int kMaxQPerKv = 8;
 constexpr int kMaxTopK = 64;         // fused top-k width
 constexpr int kAttTile = 16;         // positions per attention tile
+constexpr int kMaxChunks = 32;       // split-KV chunks per (row, kv head); one warp lane each in the combine
 
 enum PhaseKind : int { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_D = 4, PH_LMH = 5, PH_SAMPLE = 6 };
 
@@ -57,7 +58,9 @@ struct DecodeParams {
     int32_t xs_floats;  // floats reserved for the activation stage in shared memory
     int32_t step_t;     // token index within mg_prefill/mg_embed (row active iff step_t < nvalid[b])
     int32_t ids_ld;
-    int32_t pad0_;
+    int32_t max_inflight;  // weight/KV tiles a CTA keeps in flight (<= S); bounds memory-queue latency
+    int32_t pf_tiles;      // how far (tiles) the producer prefetches into L2 ahead of its ring loads
+    int32_t pad2_;
 
     const LayerPtrs *layers;
     const void *lm_head;   // [V][Hp]
@@ -92,8 +95,52 @@ struct DecodeParams {
     uint32_t *err;    // device error word
     int32_t n_phases;
     int32_t pad1_;
+    // optional timeline: [G][n_phases][kTraceSlots] %globaltimer stamps, then [G][2] kernel begin/end
+    uint64_t *trace;
 };
 
+// trace slots per (CTA, phase)
+constexpr int kTraceSlots = 10;
+constexpr int kTrAttLoaded = 6;   // attention: raw q/k/v in shared memory (first item)
+constexpr int kTrAttRoped = 7;    // attention: QK-norm + RoPE done (first item)
+constexpr int kTrAttTiles = 8;    // attention: all tiles of the first item done
+constexpr int kTrAttPart = 9;     // attention: partial of the first item written
+constexpr int kTrStart = 0;      // consumer reaches the phase
+constexpr int kTrReady = 1;      // its input dependency is satisfied
+constexpr int kTrPrologue = 2;   // input vector staged in shared memory
+constexpr int kTrEnd = 3;        // phase done and signalled
+constexpr int kTrProdStart = 4;  // producer starts issuing this phase's tiles
+constexpr int kTrProdEnd = 5;    // producer issued its last tile of the phase
+
 inline int num_phases(int L) { return 5 * L + 2; }
+
+// Tile shape of a projection matrix with padded row length Kp: tiles of `rps`
+// rows (8 warps x rows per warp) by `kc` columns; `mult` = 2 stores the gate
+// and up rows of the same output rows together.  kc divides Kp (nseg segments
+// per row) so every tile is the same size and fits one ring stage.  On the
+// device a matrix is stored tile by tile -- [row group][segment][mult*rps][kc]
+// -- so each tile is one contiguous bulk copy.
+struct TileShape {
+    int rps, mult, kc, nseg;
+};
+__host__ __device__ inline TileShape tile_shape(int Kp, int esz, bool pair) {
+    TileShape t;
+    t.rps = kConsumerWarps * (esz == 2 ? 2 : 1);
+    t.mult = pair ? 2 : 1;
+    const int per_row = t.rps * t.mult * esz;  // bytes per column of a tile
+    int n = (Kp * per_row + kStageBytes - 1) / kStageBytes;
+    if (n < 1) n = 1;
+    while (Kp % n != 0 || (Kp / n) % 8 != 0) ++n;
+    t.nseg = n;
+    t.kc = Kp / n;
+    return t;
+}
+// Elements of one tile, and of a tiled matrix with N rows.
+__host__ __device__ inline int64_t tile_elems(const TileShape &t) {
+    return static_cast<int64_t>(t.mult) * t.rps * t.kc;
+}
+__host__ __device__ inline int64_t tiled_elems(const TileShape &t, int64_t N) {
+    return (N + t.rps - 1) / t.rps * t.nseg * tile_elems(t);
+}
 
 }  // namespace mg

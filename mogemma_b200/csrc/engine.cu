@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -18,7 +19,7 @@
 #include "decode.cuh"
 
 namespace mg {
-size_t decode_smem_bytes(int S, int xs_floats);
+size_t decode_smem_bytes(int S, int xs_floats, int L);
 template <typename WT>
 size_t decode_static_smem();
 template <typename WT>
@@ -33,6 +34,9 @@ cudaError_t sample_rows_launch(const float *logits, int64_t ld, int rows, int V,
                                int32_t *tok, cudaStream_t stream);
 cudaError_t convert_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, void *dst, int dst_dtype,
                                 int64_t dst_ld, cudaStream_t stream);
+cudaError_t tile_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, int64_t row_off, void *dst,
+                             int dst_dtype, int Kp, int rps, int mult, int kc, int nseg, int part,
+                             cudaStream_t stream);
 }  // namespace mg
 
 using namespace mg;
@@ -101,6 +105,10 @@ struct mg_model {
     size_t sync_words = 0;
     std::vector<int32_t> h_pos;
     int32_t *pinned = nullptr;  // pinned staging for small transfers
+    uint64_t *trace = nullptr;  // decode timeline (mg_trace_enable)
+    bool trace_on = false;
+    int max_inflight = 2;       // outstanding bulk copies per CTA (MOGEMMA_B200_INFLIGHT)
+    int pf_tiles = 0;           // L2 prefetch distance in tiles (MOGEMMA_B200_PREFETCH)
 };
 
 template <typename T>
@@ -164,6 +172,26 @@ static mg_status upload_matrix(mg_model *m, const Desc &d, int64_t rows, int64_t
                            cudaMemcpyHostToDevice, m->stream));
         CU(convert_rows_launch(staging, d.dtype, nr, cols, static_cast<char *>(dst) + r0 * dst_ld * dsize(dst_dtype),
                                dst_dtype, dst_ld, m->stream));
+    }
+    return MG_OK;
+}
+
+// Upload rows [0, rows) of a [rows, cols] host tensor as rows
+// [row_off, row_off + rows) of a tiled device matrix (see tile_shape); `part`
+// selects the gate (0) or up (1) block of gate/up tiles.
+static mg_status upload_tiled(mg_model *m, const Desc &d, int64_t rows, int64_t cols, int64_t row_off, void *dst,
+                              int dst_dtype, int Kp, const TileShape &sh, int part, void *staging,
+                              size_t staging_bytes) {
+    if (d.dtype != MG_F32 && d.dtype != MG_BF16)
+        return fail(MG_ERR_INVALID, "unsupported weight dtype %d (expected F32 or BF16)", d.dtype);
+    const size_t row_bytes = static_cast<size_t>(cols) * dsize(d.dtype);
+    const int64_t rows_per = std::max<int64_t>(1, static_cast<int64_t>(staging_bytes / std::max<size_t>(row_bytes, 1)));
+    for (int64_t r0 = 0; r0 < rows; r0 += rows_per) {
+        const int64_t nr = std::min(rows_per, rows - r0);
+        CU(cudaMemcpyAsync(staging, static_cast<const char *>(d.data) + r0 * row_bytes, nr * row_bytes,
+                           cudaMemcpyHostToDevice, m->stream));
+        CU(tile_rows_launch(staging, d.dtype, nr, cols, row_off + r0, dst, dst_dtype, Kp, sh.rps, sh.mult, sh.kc,
+                            sh.nseg, part, m->stream));
     }
     return MG_OK;
 }
@@ -286,8 +314,13 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     CU(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->dev));
     const int Kmax = std::max(m->Hp, std::max(m->Ap, m->Ip));
     const int Gq = m->Hq / m->Hkv;
+    // shared activation stage: GEMV inputs; o_proj input + split-KV weights;
+    // attention scratch; top-k selection scratch
     int xs = m->Bmax * Kmax;
-    xs = std::max(xs, Gq * hd + 2 * hd + Gq * kAttTile + 3 * kMaxQPerKv + 8);
+    xs = std::max(xs, m->Bmax * (m->Hp + m->H));  // normed input + staged residual rows
+    xs = std::max(xs, m->Bmax * (m->Ap + m->Hq * kMaxChunks));
+    xs = std::max(xs, (Gq + 2) * hd + Gq * kAttTile + 3 * kMaxQPerKv + 2 * hd + m->Bmax * hd +
+                          kConsumerThreads * Gq + 8);
     xs = std::max(xs, static_cast<int>((sizeof(uint32_t) * 264 + sizeof(uint64_t) * 1024 + kMaxTopK * 8 * 2 +
                                         kMaxTopK * 4) / 4 + 16));
     m->xs_floats = (xs + 31) / 32 * 32;
@@ -295,14 +328,14 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         (m->wdtype == MG_F32 ? decode_static_smem<float>() : decode_static_smem<__nv_bfloat16>()) + 64;
     m->S = 0;
     for (int S = 8; S >= 2; --S)
-        if (decode_smem_bytes(S, m->xs_floats) + static_smem <= static_cast<size_t>(max_smem)) {
+        if (decode_smem_bytes(S, m->xs_floats, L) + static_smem <= static_cast<size_t>(max_smem)) {
             m->S = S;
             break;
         }
     if (m->S < 2)
         return fail(MG_ERR_UNSUPPORTED, "activation stage of %d floats leaves no room for the weight ring",
                     m->xs_floats);
-    m->smem = decode_smem_bytes(m->S, m->xs_floats);
+    m->smem = decode_smem_bytes(m->S, m->xs_floats, L);
     if (m->wdtype == MG_F32) {
         CU(decode_prepare<float>(m->smem));
     } else {
@@ -311,7 +344,9 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     const int occ = m->wdtype == MG_F32 ? decode_occupancy<float>(m->smem) : decode_occupancy<__nv_bfloat16>(m->smem);
     if (occ < 1) return fail(MG_ERR_UNSUPPORTED, "decode kernel does not fit on an SM (smem %zu)", m->smem);
     m->G = m->num_sms;  // one persistent CTA per SM
-    m->max_ch = (m->cap + kAttTile - 1) / kAttTile;
+    if (const char *e = getenv("MOGEMMA_B200_INFLIGHT")) m->max_inflight = std::max(1, atoi(e));
+    if (const char *e = getenv("MOGEMMA_B200_PREFETCH")) m->pf_tiles = std::max(0, atoi(e));
+    m->max_ch = kMaxChunks;
 
     // ---- weights
     const int wd = m->wdtype;
@@ -321,26 +356,33 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     TRY(dalloc(m, reinterpret_cast<char **>(&staging), staging_bytes, false));
     m->h_layers.resize(L);
     m->weight_bytes = 0;
+    const TileShape sh_h = tile_shape(m->Hp, static_cast<int>(we), false);   // q/k/v, lm_head
+    const TileShape sh_a = tile_shape(m->Ap, static_cast<int>(we), false);   // o_proj
+    const TileShape sh_gu = tile_shape(m->Hp, static_cast<int>(we), true);   // gate + up
+    const TileShape sh_i = tile_shape(m->Ip, static_cast<int>(we), false);   // down_proj
     for (int l = 0; l < L; ++l) {
         LayerPtrs &lp = m->h_layers[l];
-        void *qkv, *o, *gate, *up, *down;
-        TRY(dalloc(m, reinterpret_cast<char **>(&qkv), static_cast<size_t>(m->qkv_rows) * m->Hp * we));
-        TRY(dalloc(m, reinterpret_cast<char **>(&o), static_cast<size_t>(m->H) * m->Ap * we));
-        TRY(dalloc(m, reinterpret_cast<char **>(&gate), static_cast<size_t>(m->I) * m->Hp * we));
-        TRY(dalloc(m, reinterpret_cast<char **>(&up), static_cast<size_t>(m->I) * m->Hp * we));
-        TRY(dalloc(m, reinterpret_cast<char **>(&down), static_cast<size_t>(m->H) * m->Ip * we));
+        void *qkv, *o, *gu, *down;
+        TRY(dalloc(m, reinterpret_cast<char **>(&qkv), static_cast<size_t>(tiled_elems(sh_h, m->qkv_rows)) * we));
+        TRY(dalloc(m, reinterpret_cast<char **>(&o), static_cast<size_t>(tiled_elems(sh_a, m->H)) * we));
+        TRY(dalloc(m, reinterpret_cast<char **>(&gu), static_cast<size_t>(tiled_elems(sh_gu, m->I)) * we));
+        TRY(dalloc(m, reinterpret_cast<char **>(&down), static_cast<size_t>(tiled_elems(sh_i, m->H)) * we));
         const int64_t kvr = static_cast<int64_t>(m->Hkv) * hd;
-        TRY(upload_matrix(m, *lw(l, "self_attn.q_proj.weight"), m->A, m->H, qkv, wd, m->Hp, staging, staging_bytes));
-        TRY(upload_matrix(m, *lw(l, "self_attn.k_proj.weight"), kvr, m->H,
-                          static_cast<char *>(qkv) + static_cast<size_t>(m->A) * m->Hp * we, wd, m->Hp, staging,
-                          staging_bytes));
-        TRY(upload_matrix(m, *lw(l, "self_attn.v_proj.weight"), kvr, m->H,
-                          static_cast<char *>(qkv) + static_cast<size_t>(m->A + kvr) * m->Hp * we, wd, m->Hp,
-                          staging, staging_bytes));
-        TRY(upload_matrix(m, *lw(l, "self_attn.o_proj.weight"), m->H, m->A, o, wd, m->Ap, staging, staging_bytes));
-        TRY(upload_matrix(m, *lw(l, "mlp.gate_proj.weight"), m->I, m->H, gate, wd, m->Hp, staging, staging_bytes));
-        TRY(upload_matrix(m, *lw(l, "mlp.up_proj.weight"), m->I, m->H, up, wd, m->Hp, staging, staging_bytes));
-        TRY(upload_matrix(m, *lw(l, "mlp.down_proj.weight"), m->H, m->I, down, wd, m->Ip, staging, staging_bytes));
+        TRY(upload_tiled(m, *lw(l, "self_attn.q_proj.weight"), m->A, m->H, 0, qkv, wd, m->Hp, sh_h, 0, staging,
+                         staging_bytes));
+        TRY(upload_tiled(m, *lw(l, "self_attn.k_proj.weight"), kvr, m->H, m->A, qkv, wd, m->Hp, sh_h, 0, staging,
+                         staging_bytes));
+        TRY(upload_tiled(m, *lw(l, "self_attn.v_proj.weight"), kvr, m->H, m->A + kvr, qkv, wd, m->Hp, sh_h, 0,
+                         staging, staging_bytes));
+        TRY(upload_tiled(m, *lw(l, "self_attn.o_proj.weight"), m->H, m->A, 0, o, wd, m->Ap, sh_a, 0, staging,
+                         staging_bytes));
+        TRY(upload_tiled(m, *lw(l, "mlp.gate_proj.weight"), m->I, m->H, 0, gu, wd, m->Hp, sh_gu, 0, staging,
+                         staging_bytes));
+        TRY(upload_tiled(m, *lw(l, "mlp.up_proj.weight"), m->I, m->H, 0, gu, wd, m->Hp, sh_gu, 1, staging,
+                         staging_bytes));
+        TRY(upload_tiled(m, *lw(l, "mlp.down_proj.weight"), m->H, m->I, 0, down, wd, m->Ip, sh_i, 0, staging,
+                         staging_bytes));
+        void *gate = gu, *up = nullptr;
         m->weight_bytes += static_cast<int64_t>(we) * (static_cast<int64_t>(m->qkv_rows) * m->H +
                                                         static_cast<int64_t>(m->H) * m->A +
                                                         3 * static_cast<int64_t>(m->I) * m->H);
@@ -373,16 +415,14 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         lp.k_norm = norms[5];
         lp.is_global = (m->mode == 0) ? 1 : (((l + 1) % m->global_every) == 0 ? 1 : 0);
     }
-    TRY(dalloc(m, reinterpret_cast<char **>(&m->lm_head), static_cast<size_t>(m->V) * m->Hp * we));
-    TRY(upload_matrix(m, *lmh, m->V, m->H, m->lm_head, wd, m->Hp, staging, staging_bytes));
+    TRY(dalloc(m, reinterpret_cast<char **>(&m->lm_head), static_cast<size_t>(tiled_elems(sh_h, m->V)) * we));
+    TRY(upload_tiled(m, *lmh, m->V, m->H, 0, m->lm_head, wd, m->Hp, sh_h, 0, staging, staging_bytes));
     m->weight_bytes += static_cast<int64_t>(we) * m->V * m->H;
-    if (emb->data == lmh->data && emb->dtype == lmh->dtype) {
-        m->embed = m->lm_head;  // tied (convert.py:129-131 writes lm_head as a copy of the embedding)
-    } else {
-        TRY(dalloc(m, reinterpret_cast<char **>(&m->embed), static_cast<size_t>(m->V) * m->Hp * we));
-        TRY(upload_matrix(m, *emb, m->V, m->H, m->embed, wd, m->Hp, staging, staging_bytes));
-    }
-    m->embed_ld = m->Hp;
+    // embedding rows are gathered, so they stay row-major (a separate copy even
+    // when lm_head is tied to them, convert.py:129-131)
+    TRY(dalloc(m, reinterpret_cast<char **>(&m->embed), static_cast<size_t>(m->V) * m->H * we));
+    TRY(upload_matrix(m, *emb, m->V, m->H, m->embed, wd, m->H, staging, staging_bytes));
+    m->embed_ld = m->H;
     TRY(dalloc(m, &m->final_norm, m->H));
     TRY(upload_matrix(m, *fnorm, 1, m->H, m->final_norm, MG_F32, m->H, staging, staging_bytes));
     TRY(dalloc(m, &m->d_layers, L));
@@ -430,7 +470,7 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     TRY(dalloc(m, &m->tok, kMaxRows));
     TRY(dalloc(m, &m->pos, kMaxRows));
     TRY(dalloc(m, &m->uniforms, kMaxRows));
-    m->sync_words = num_phases(L) + L + kMaxRows * m->Hkv + 1;
+    m->sync_words = num_phases(L) + 1;
     TRY(dalloc(m, &m->sync, m->sync_words));
     TRY(dalloc(m, &m->err, 1));
     CU(cudaMallocHost(&m->pinned, 4096));
@@ -531,20 +571,22 @@ static DecodeParams base_params(mg_model *m, int B) {
     p.seed = m->seed;
     p.sync = m->sync;
     p.err = m->err;
+    p.max_inflight = m->max_inflight;
+    p.pf_tiles = m->pf_tiles;
+    p.trace = m->trace_on ? m->trace : nullptr;
     p.n_phases = num_phases(m->L);
     p.ph_begin = 0;
     p.ph_end = p.n_phases;
     return p;
 }
 
-// Chunk size for split-KV attention: about `target` chunks per (row, kv head).
+// Positions per split-KV chunk: about 16 chunks per (row, kv head), never more
+// than kMaxChunks for the longest row of the launch, whole tiles.
 static int att_chunk(const mg_model *m, int B, int max_ctx) {
-    const int target = std::max(1, std::min(32, m->G / std::max(1, B * m->Hkv)));
-    int ch = (max_ctx + target - 1) / target;
+    const int target = std::max(1, std::min(16, m->G / std::max(1, B * m->Hkv)));
+    int ch = std::max((max_ctx + target - 1) / target, (max_ctx + kMaxChunks - 1) / kMaxChunks);
     ch = (ch + kAttTile - 1) / kAttTile * kAttTile;
-    ch = std::max(ch, kAttTile);
-    const int min_ch = (m->cap + m->max_ch - 1) / m->max_ch;
-    return std::max(ch, (min_ch + kAttTile - 1) / kAttTile * kAttTile);
+    return std::max(ch, kAttTile);
 }
 
 static mg_status run_decode(mg_model *m, DecodeParams &p, int max_ctx) {
@@ -884,6 +926,29 @@ extern "C" mg_status mg_sample(const float *logits_host, int32_t batch, int32_t 
     cudaFree(dout);
     if (du) cudaFree(du);
     if (e != cudaSuccess) return fail(MG_ERR_CUDA, "mg_sample: %s", cudaGetErrorString(e));
+    return MG_OK;
+}
+
+static size_t trace_words(const mg_model *m) {
+    return static_cast<size_t>(m->G) * num_phases(m->L) * kTraceSlots + 2 * static_cast<size_t>(m->G);
+}
+
+extern "C" mg_status mg_trace_enable(mg_model *m, int32_t on) {
+    if (!m) return fail(MG_ERR_INVALID, "null model");
+    CU(cudaSetDevice(m->dev));
+    if (on && !m->trace) TRY(dalloc(m, &m->trace, trace_words(m)));
+    m->trace_on = on != 0;
+    return MG_OK;
+}
+
+extern "C" mg_status mg_trace_read(mg_model *m, uint64_t *out_host, int64_t capacity, int64_t *n_out) {
+    if (!m || !out_host || !n_out) return fail(MG_ERR_INVALID, "null argument");
+    if (!m->trace) return fail(MG_ERR_INVALID, "tracing was never enabled");
+    const size_t n = std::min(trace_words(m), static_cast<size_t>(capacity));
+    CU(cudaSetDevice(m->dev));
+    CU(cudaStreamSynchronize(m->stream));
+    CU(cudaMemcpy(out_host, m->trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+    *n_out = static_cast<int64_t>(trace_words(m));
     return MG_OK;
 }
 
