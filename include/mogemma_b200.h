@@ -148,6 +148,28 @@ mg_status mg_set_tokens(mg_model *m, const int32_t *token_ids_host, int32_t batc
 mg_status mg_sample(const float *logits_host, int32_t batch, int32_t vocab, const mg_sampling *s, uint64_t seed,
                     uint64_t offset, int32_t *out_host);
 
+/* ---- sampling over device logits without allocating (no counterpart in the
+ * reference, whose sampler is numpy on the host) ----
+ * For callers that own all device memory through their own pool and must not
+ * see cudaMalloc/cudaFree in their steady state (those calls synchronise the
+ * whole device).  Draws one token per row of logits_dev ([batch] rows of
+ * `vocab` floats, row stride `ld`, device memory) into out_dev (device memory),
+ * asynchronously on `stream` (a cudaStream_t; NULL: the legacy default stream),
+ * with the rules and the Philox stream of mg_sample: same arguments, same
+ * tokens.  uniforms_dev (nullable) is a device array of [batch] variates.
+ * Limits: batch <= MG_SAMPLE_STATIC_MAX_ROWS, and temperature <= 0 or
+ * 0 < top_k <= 64 (MG_ERR_INVALID / MG_ERR_UNSUPPORTED beyond).  Its only
+ * scratch is a static device array of 8 * 148 * 64 candidate keys (606,208
+ * bytes) shared by every call on a device: calls that overlap on the GPU race;
+ * calls on one stream are safe.  The first call on a device (the current one)
+ * resolves the array's address and a kernel attribute; make it before any
+ * stream capture. */
+#define MG_SAMPLE_STATIC_MAX_ROWS 8
+#define MG_SAMPLE_STATIC_MAX_SLICES 148
+mg_status mg_sample_static(const float *logits_dev, int64_t ld, int32_t batch, int32_t vocab, double temperature,
+                           int32_t top_k, double top_p, const double *uniforms_dev, uint64_t seed, uint64_t offset,
+                           int32_t *out_dev, void *stream);
+
 /* ---- embeddings ----
  * Mean of final-normed hidden states per sequence (forward_sequence,
  * layers.mojo:292-370), ids row-major [batch, max_len] with lens_host[b] valid. */

@@ -71,6 +71,11 @@ static mg_status fail(mg_status st, const char *fmt, ...) {
 extern "C" const char *mg_last_error(void) { return g_err.c_str(); }
 extern "C" int32_t mg_abi_version(void) { return MG_ABI_VERSION; }
 
+// Error reporting for entry points defined in other translation units.
+namespace mg {
+mg_status report_error(mg_status st, const char *msg) { return fail(st, "%s", msg); }
+}  // namespace mg
+
 // ---------------------------------------------------------------- model
 struct mg_model {
     int dev = 0;
