@@ -189,7 +189,7 @@ def run_reference(args, world: int, rank: int) -> None:
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, uniform random ids)",
-        "config": {"workload": "Gemma3-1B batch-1 decode (fp32 weights)", "global_batch": 1, "seq_len": PROMPT + DECODE,
+        "config": {"workload": f"{CONFIG} batch-1 decode (fp32 weights)", "global_batch": 1, "seq_len": PROMPT + DECODE,
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{per_step} decode steps per step on {threads} threads (OpenMP over output rows; "
@@ -200,6 +200,7 @@ def run_reference(args, world: int, rank: int) -> None:
 
 
 def main() -> None:
+    global CONFIG, PROMPT, DECODE  # noqa: PLW0603
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -208,7 +209,11 @@ def main() -> None:
     ap.add_argument("--weight-dtype", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--cpu-sample", type=int, default=25)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model", default=CONFIG, help="synthetic config (gemma3-270m for small profiling runs)")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled before the timed decode")
+    ap.add_argument("--decode", type=int, default=DECODE, help="tokens decoded per step")
     args = ap.parse_args()
+    CONFIG, PROMPT, DECODE = args.model, args.prompt, args.decode
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)
@@ -292,7 +297,7 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": args.weight_dtype,
             "data": "synthetic (seeded N(0,0.02) random-init weights, uniform random prompt ids)",
-            "config": {"workload": f"Gemma3-1B batch-1 decode: {PROMPT}-token prompt then {DECODE} tokens "
+            "config": {"workload": f"{CONFIG} batch-1 decode: {PROMPT}-token prompt then {DECODE} tokens "
                                    f"(T={TEMPERATURE}, top-k {TOP_K}), {args.weight_dtype} weights",
                        "model": CONFIG, "global_batch": world, "seq_len": PROMPT + DECODE,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",

@@ -163,6 +163,8 @@ struct Smem {
 };
 
 struct SmallSmem {
+    AttRows att;    // consumers' split of the current attention phase
+    AttRows att_p;  // the producer's (it runs phases ahead)
     int pos[kMaxRows];
     int tok[kMaxRows];
     int active[kMaxRows];
@@ -224,7 +226,7 @@ __device__ __forceinline__ void norm_prefetch(NormW &nw, const float *w_add, con
 // (when out != null);  xs[b] <- rmsnorm(x) * (1 + w_next), zero padded to Kp.
 // base/add rows ([B][H] in global memory) were written by other CTAs and are
 // read through L2; all loads of a chunk are issued before any is used.
-__device__ __noinline__ void stage_norm(const float *base, const float *add, const float *w_add,
+__device__ __forceinline__ void stage_norm(const float *base, const float *add, const float *w_add,
                                         const float *w_next, const NormW &nw, float *out, int H, int Kp, int B,
                                         float *xs, SmallSmem &ss, int tid, uint64_t *tr = nullptr) {
     float sq[kMaxRows], sq2[kMaxRows];
@@ -483,10 +485,18 @@ __device__ __forceinline__ void gemv_consume(const GemvGeom<WT> &g, int B, const
 // partial (m, l, acc) per (row, kv head, chunk).  Returns the item count.
 // HD (head dim) and GQ (q heads per kv head) are compile-time when non-zero so
 // every loop unrolls and its shared/global loads issue together.
+// Result of a CTA's attention items: partials written, and the consumer's
+// ring position and status afterwards (returned by value so that nothing of
+// the caller has to live in local memory across the call).
+struct AttRet {
+    uint32_t done, tile;
+    bool ok;
+};
+
 template <int HD, int GQ>
-__device__ __noinline__ uint32_t att_items(const DecodeParams &p, const Smem &sm, SmallSmem &ss, const LayerPtrs &lp,
-                                           int layer, int ph, const AttRows &a, uint32_t &tile, bool &ok, int tid,
-                                           bool has_dep) {
+__device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, SmallSmem &ss, const LayerPtrs &lp,
+                                         int layer, int ph, const AttRows &a, uint32_t tile, bool ok, int tid,
+                                         bool has_dep) {
     constexpr int kQ = GQ ? GQ : kMaxQPerKv;         // accumulator slots
     constexpr int kDL = HD ? HD / 32 : kMaxHeadDim / 32;  // head dims per lane
     const int G = gridDim.x;
@@ -726,12 +736,12 @@ __device__ __noinline__ uint32_t att_items(const DecodeParams &p, const Smem &sm
         if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttPart));
         ++done;
     }
-    return done;
+    return AttRet{done, tile, ok};
 }
 
-__device__ __forceinline__ uint32_t att_dispatch(const DecodeParams &p, const Smem &sm, SmallSmem &ss,
-                                                 const LayerPtrs &lp, int layer, int ph, const AttRows &a,
-                                                 uint32_t &tile, bool &ok, int tid, bool has_dep) {
+__device__ __forceinline__ AttRet att_dispatch(const DecodeParams &p, const Smem &sm, SmallSmem &ss,
+                                               const LayerPtrs &lp, int layer, int ph, const AttRows &a,
+                                               uint32_t tile, bool ok, int tid, bool has_dep) {
     const int Gq = p.Hq / p.Hkv;
 #define MG_ATT(HD_, GQ_) \
     if (p.hd == HD_ && Gq == GQ_) return att_items<HD_, GQ_>(p, sm, ss, lp, layer, ph, a, tile, ok, tid, has_dep);
@@ -915,15 +925,18 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                              GemvOut{p.qkv, p.qkv_rows});
             cta_signal(ctr_phase(p, ph), 1u, ss, tid);
         } else if (kind == PH_ATT) {
-            AttRows a;
-            att_rows(p, lp.is_global != 0, ss.pos, a);
-            const uint32_t done = att_dispatch(p, sm, ss, lp, layer, ph, a, tile, ok, tid, has_dep);
-            cta_signal(ctr_phase(p, ph), done, ss, tid);
+            if (tid == 0) att_rows(p, lp.is_global != 0, ss.pos, ss.att);
+            consumer_sync(kConsumerThreads);
+            const AttRet r = att_dispatch(p, sm, ss, lp, layer, ph, ss.att, tile, ok, tid, has_dep);
+            tile = r.tile;
+            ok = r.ok;
+            cta_signal(ctr_phase(p, ph), r.done, ss, tid);
         } else if (kind == PH_O) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
-            AttRows a;
-            att_rows(p, lp.is_global != 0, ss.pos, a);
+            if (tid == 0) att_rows(p, lp.is_global != 0, ss.pos, ss.att);
+            consumer_sync(kConsumerThreads);
+            const AttRows &a = ss.att;
             if (has_dep)
                 ok = cta_wait(ctr_phase(p, ph - 1), static_cast<uint32_t>(a.nitems), p.err, 100 + ph, ss, tid) && ok;
             att_combine(p, a, g.Kp, sm.xs, tid);
@@ -1014,7 +1027,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
 
 // ---------------------------------------------------------------- producer
 template <typename WT>
-__device__ void producer_run(const DecodeParams &p, const Smem &sm, const SmallSmem &ss) {
+__device__ void producer_run(const DecodeParams &p, const Smem &sm, SmallSmem &ss) {
     const int G = gridDim.x;
     const uint64_t pol_w = policy_evict_first();
     uint32_t tile = 0, issued = 0;
@@ -1037,7 +1050,7 @@ __device__ void producer_run(const DecodeParams &p, const Smem &sm, const SmallS
         const LayerPtrs &lp = sm.layers[layer];
         trace_mark(trace_slot(p, ph, kTrProdStart));
         if (kind == PH_ATT) {
-            AttRows a;
+            AttRows &a = ss.att_p;
             att_rows(p, lp.is_global != 0, ss.pos, a);
             const int slot = cta_slot(ph);
             for (int item = slot; item < a.nitems; item += G) {
@@ -1105,32 +1118,36 @@ __device__ void producer_run(const DecodeParams &p, const Smem &sm, const SmallS
 
 // ---------------------------------------------------------------- the kernel
 template <typename WT>
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ SmallSmem ss;
-    Smem sm;
+    // The pointer block lives in shared memory: helpers take it by reference,
+    // and a local copy would turn each of their reads into a local-memory load.
+    __shared__ Smem sm;
+    Smem sl;
     {
         uintptr_t base = reinterpret_cast<uintptr_t>(smem_raw);
         base = (base + 127) & ~static_cast<uintptr_t>(127);
-        sm.ring = reinterpret_cast<unsigned char *>(base);
-        sm.xs = reinterpret_cast<float *>(sm.ring + static_cast<size_t>(p.S) * kStageBytes);
-        sm.full = reinterpret_cast<uint64_t *>(sm.xs + p.xs_floats);
-        sm.empty = sm.full + p.S;
-        sm.layers = reinterpret_cast<LayerPtrs *>(sm.empty + p.S);
+        sl.ring = reinterpret_cast<unsigned char *>(base);
+        sl.xs = reinterpret_cast<float *>(sl.ring + static_cast<size_t>(p.S) * kStageBytes);
+        sl.full = reinterpret_cast<uint64_t *>(sl.xs + p.xs_floats);
+        sl.empty = sl.full + p.S;
+        sl.layers = reinterpret_cast<LayerPtrs *>(sl.empty + p.S);
     }
+    if (threadIdx.x == 0) sm = sl;
     const int tid = threadIdx.x;
     const int G = gridDim.x;
 
     if (tid == 0) {
         for (int s = 0; s < p.S; ++s) {
-            mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], kConsumerWarps);
+            mbar_init(&sl.full[s], 1);
+            mbar_init(&sl.empty[s], kConsumerWarps);
         }
         fence_barrier_init();
     }
     {
         const uint32_t *src = reinterpret_cast<const uint32_t *>(p.layers);
-        uint32_t *dst = reinterpret_cast<uint32_t *>(sm.layers);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(sl.layers);
         const int nw = p.L * static_cast<int>(sizeof(LayerPtrs) / 4);
         for (int i = tid; i < nw; i += kThreads) dst[i] = src[i];
     }
