@@ -56,14 +56,17 @@ __device__ __forceinline__ bool wait_counter_geq(const uint32_t *ctr, uint32_t t
                                                  uint32_t site) {
     if (ld_acquire_u32(ctr) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (true) {
+    for (uint32_t n = 1;; ++n) {
         if (ld_acquire_u32(ctr) >= target) return true;
-        if (ld_relaxed_u32(err) != 0u) return false;
-        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
-            set_error(err, kErrTimeoutCounter | site);
-            return false;
+        // the error word and the clock are checked every 8th poll: each check
+        // is another dependent round trip between two polls
+        if ((n & 7u) == 0u) {
+            if (ld_relaxed_u32(err) != 0u) return false;
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+                set_error(err, kErrTimeoutCounter | site);
+                return false;
+            }
         }
-        __nanosleep(20);
     }
 }
 
@@ -168,6 +171,14 @@ __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
+// 1 / sqrt(sum * inv_n + 1e-6): the scale of an RMSNorm (ops.mojo:98-136),
+// through rsqrt.approx (relative error about 1e-7) rather than the IEEE divide
+// and square root, whose sequence sat on the critical path of every norm
+// prologue (about 1.6 us each, measured).  The reference's own sum order
+// differs from any parallel one, so parity is a tolerance in any case.
+__device__ __forceinline__ float rms_inv(float sum, float inv_n) { return rsqrtf(sum * inv_n + 1e-6f); }
+constexpr float kInvSqrt2 = 0.70710678118654752f;  // GeGLU: erf(g / sqrt 2) as erf(g * (1 / sqrt 2))
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -220,6 +220,10 @@ __device__ __forceinline__ void norm_prefetch(NormW &nw, const float *w_add, con
         nw.wa[j] = (w_add != nullptr && i < H) ? __ldg(w_add + i) : 0.f;
         nw.wn[j] = (w_next != nullptr && i < H) ? __ldg(w_next + i) : 0.f;
     }
+    // Pin the loads here: without this the compiler may sink them past the
+    // dependency wait, onto the prologue's critical path.
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) asm volatile("" : "+f"(nw.wa[j]), "+f"(nw.wn[j]));
 }
 
 // For rows b < B:  x = base[b] + rmsnorm(add[b]) * (1 + w_add);  out[b] <- x
@@ -227,9 +231,13 @@ __device__ __forceinline__ void norm_prefetch(NormW &nw, const float *w_add, con
 // base/add rows ([B][H] in global memory) were written by other CTAs and are
 // read through L2; all loads of a chunk are issued before any is used.
 __device__ __forceinline__ void stage_norm(const float *base, const float *add, const float *w_add,
-                                        const float *w_next, const NormW &nw, float *out, int H, int Kp, int B,
+                                        const float *w_next, const NormW &nw, float *out, int H, float inv_h, int Kp,
+                                        int B,
                                         float *xs, SmallSmem &ss, int tid, uint64_t *tr = nullptr) {
     float sq[kMaxRows], sq2[kMaxRows];
+    uint64_t *xt = tr ? tr - 6 : nullptr;
+#define XS(k) if (xt && tid == 0) xt[k] = clock64();
+    XS(12)
 #pragma unroll
     for (int b = 0; b < kMaxRows; ++b) sq[b] = sq2[b] = 0.f;
     float *xb = xs + B * Kp;  // base rows staged next to the activation stage
@@ -257,8 +265,10 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
                 if (bb == b) sq[bb] += s;
         }
     }
+    XS(13)
     if (tr && tid == 0) trace_mark(tr);
     block_sum_rows(sq, B, ss, tid);
+    XS(14)
     if (tr && tid == 0) trace_mark(tr + 1);
     // The first chunk uses the prefetched weights; later chunks (H > 2048) load
     // theirs.  Separate branches keep the first chunk free of global loads.
@@ -277,7 +287,7 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
 #pragma unroll
         for (int b = 0; b < kMaxRows; ++b) {
             if (b >= B) break;
-            const float inv = 1.0f / sqrtf(sq[b] / static_cast<float>(H) + 1e-6f);
+            const float inv = rms_inv(sq[b], inv_h);
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
                 const int i = tid + (j0 + j) * kConsumerThreads;
@@ -290,7 +300,9 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
             }
         }
     }
+    XS(15)
     block_sum_rows(sq2, B, ss, tid);
+    XS(16)
     if (tr && tid == 0) trace_mark(tr + 2);
     for (int j0 = 0; j0 * kConsumerThreads < Kp; j0 += kNormPer) {
         float wn[kNormPer];
@@ -307,7 +319,7 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
 #pragma unroll
         for (int b = 0; b < kMaxRows; ++b) {
             if (b >= B) break;
-            const float inv = 1.0f / sqrtf(sq2[b] / static_cast<float>(H) + 1e-6f);
+            const float inv = rms_inv(sq2[b], inv_h);
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
                 const int i = tid + (j0 + j) * kConsumerThreads;
@@ -315,15 +327,18 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
             }
         }
     }
+    XS(17)
     consumer_sync(kConsumerThreads);
+    XS(18)
+#undef XS
 }
 
 // Layer 0 input: x = E[tok] * sqrt(H) (model.mojo:62-68, layers.mojo:247-251),
 // out <- x, xs <- rmsnorm(x) * (1 + w).
 template <typename WT>
 __device__ __noinline__ void stage_embed(const WT *E, int64_t ld, const int *toks, const float *w, float *out,
-                                         int H, int Kp, int B, float *xs, SmallSmem &ss, int tid) {
-    const float scale = sqrtf(static_cast<float>(H));
+                                         int H, float inv_h, float scale, int Kp, int B, float *xs, SmallSmem &ss,
+                                         int tid) {
     float sq[kMaxRows];
 #pragma unroll
     for (int b = 0; b < kMaxRows; ++b) {
@@ -344,7 +359,7 @@ __device__ __noinline__ void stage_embed(const WT *E, int64_t ld, const int *tok
 #pragma unroll
         for (int bb = 0; bb < kMaxRows; ++bb)
             if (bb == b) s = sq[bb];
-        const float inv = 1.0f / sqrtf(s / static_cast<float>(H) + 1e-6f);
+        const float inv = rms_inv(s, inv_h);
         for (int i = tid; i < Kp; i += kConsumerThreads) xs[b * Kp + i] = i < H ? xs[b * Kp + i] * inv * (1.0f + w[i]) : 0.f;
     }
     consumer_sync(kConsumerThreads);
@@ -354,10 +369,9 @@ __device__ __noinline__ void stage_embed(const WT *E, int64_t ld, const int *tok
 __device__ __forceinline__ void cta_signal(uint32_t *ctr, uint32_t n, SmallSmem &ss, int tid) {
     consumer_sync(kConsumerThreads);
     if (tid == 0) {
-        if (n) {
-            fence_acq_rel_gpu();
-            red_release_add_u32(ctr, n);
-        }
+        // The barrier orders every consumer's writes before thread 0's release;
+        // red.release is cumulative over them at gpu scope.
+        if (n) red_release_add_u32(ctr, n);
         trace_mark(ss.tr_end);
     }
 }
@@ -403,8 +417,10 @@ __device__ __forceinline__ void gemv_tiles(const GemvGeom<WT> &g, const float *_
         for (int s = 0; s < g.nseg; ++s, ++tile) {
             const int st = static_cast<int>(tile % S);
             const uint32_t par = (tile / S) & 1u;
+            if (grp == 0 && s == 0 && tid == 0 && tr_first) tr_first[19 - 2] = clock64();
             if (ok) ok = mbar_wait(&sm.full[st], par, err, kErrTimeoutFull | 1u);
             if (grp == 0 && s == 0 && tid == 0) trace_mark(tr_first);
+            if (grp == 0 && s == 0 && tid == 0 && tr_first) tr_first[20 - 2] = clock64();
             const int c0 = s * g.kc;
             const int sw = min(g.kc, Kp - c0);
             const WT *stage = reinterpret_cast<const WT *>(sm.ring + static_cast<size_t>(st) * kStageBytes);
@@ -432,6 +448,7 @@ __device__ __forceinline__ void gemv_tiles(const GemvGeom<WT> &g, const float *_
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[st]);
+            if (grp == 0 && s == 0 && tid == 0 && tr_first) tr_first[21 - 2] = clock64();
         }
 #pragma unroll
         for (int k = 0; k < rpw; ++k) {
@@ -442,7 +459,7 @@ __device__ __forceinline__ void gemv_tiles(const GemvGeom<WT> &g, const float *_
                 if constexpr (PAIR) {
                     const float u = warp_sum(acc2[k][b]);
                     if (lane == 0 && j < nr && ok) {
-                        const float gelu = 0.5f * d * (1.0f + erff(d / 1.4142135623730951f));
+                        const float gelu = 0.5f * d * (1.0f + erff(d * kInvSqrt2));
                         o.out[b * o.ld + g.row0 + grp * g.rps + j] = gelu * u;
                     }
                 } else {
@@ -532,7 +549,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
         }
     }
     if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
-    const float scale = 1.0f / sqrtf(static_cast<float>(hd));
+    const float scale = p.att_scale;
     const int slot = cta_slot(ph);
     uint32_t done = 0;
     for (int item = slot; item < a.nitems; item += G) {
@@ -583,7 +600,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
                     if (d < hd) s += x[d] * x[d];
                 }
                 s = warp_sum(s);
-                const float inv = 1.0f / sqrtf(s / static_cast<float>(hd) + 1e-6f);
+                const float inv = rms_inv(s, p.inv_hd);
 #pragma unroll
                 for (int i = 0; i < kDL; ++i) {
                     const int d = lane + 32 * i;
@@ -911,15 +928,15 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             gemv_geom<WT>(p, lp, kind, ph, g);
             float *out_h = (blockIdx.x == 0) ? p.h : nullptr;
             if (layer == 0) {
-                stage_embed<WT>(static_cast<const WT *>(p.embed), p.embed_ld, ss.tok, lp.in_ln, out_h, p.H, g.Kp, B,
-                                sm.xs, ss, tid);
+                stage_embed<WT>(static_cast<const WT *>(p.embed), p.embed_ld, ss.tok, lp.in_ln, out_h, p.H, p.inv_h,
+                                p.emb_scale, g.Kp, B, sm.xs, ss, tid);
             } else {
                 const LayerPtrs &prev = sm.layers[layer - 1];
                 NormW nw;
                 norm_prefetch(nw, prev.post_ff_ln, lp.in_ln, p.H, tid);
                 if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
                 // x = r + norm(mlp, post_ff) (layers.mojo:216-220), xs = norm(x, input_layernorm) (195)
-                stage_norm(p.r, p.mlp_raw, prev.post_ff_ln, lp.in_ln, nw, out_h, p.H, g.Kp, B, sm.xs, ss, tid);
+                stage_norm(p.r, p.mlp_raw, prev.post_ff_ln, lp.in_ln, nw, out_h, p.H, p.inv_h, g.Kp, B, sm.xs, ss, tid);
             }
             gemv_consume<WT>(g, B, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                              GemvOut{p.qkv, p.qkv_rows});
@@ -946,15 +963,20 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
         } else if (kind == PH_GU) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
+            uint64_t *xt = trace_slot(p, ph, 0);
+            if (xt && tid == 0) xt[10] = clock64();
             NormW nw;
             norm_prefetch(nw, lp.post_attn_ln, lp.pre_ff_ln, p.H, tid);
             if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+            if (xt && tid == 0) xt[11] = clock64();
             // r = h + norm(o_raw, post_attn) (layers.mojo:202-207); xs = norm(r, pre_ff) (209-210)
-            stage_norm(p.h, p.o_raw, lp.post_attn_ln, lp.pre_ff_ln, nw, blockIdx.x == 0 ? p.r : nullptr, p.H, g.Kp, B,
+            stage_norm(p.h, p.o_raw, lp.post_attn_ln, lp.pre_ff_ln, nw, blockIdx.x == 0 ? p.r : nullptr, p.H, p.inv_h, g.Kp, B,
                        sm.xs, ss, tid, trace_slot(p, ph, 6));
             gemv_consume<WT>(g, B, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                              GemvOut{p.act, p.Ip});
+            if (xt && tid == 0) xt[22] = clock64();
             cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+            if (xt && tid == 0) xt[23] = clock64();
         } else if (kind == PH_D) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
@@ -988,7 +1010,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                 norm_prefetch(nw, lp.post_ff_ln, p.final_norm, p.H, tid);
                 if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
                 // x = r + norm(mlp_raw, post_ff); xs = norm(x, final norm) (layers.mojo:283-285)
-                stage_norm(p.r, p.mlp_raw, lp.post_ff_ln, p.final_norm, nw, nullptr, p.H, g.Kp, B, sm.xs, ss, tid);
+                stage_norm(p.r, p.mlp_raw, lp.post_ff_ln, p.final_norm, nw, nullptr, p.H, p.inv_h, g.Kp, B, sm.xs, ss, tid);
             }
             if (p.lm_mode == kLmEmbed) {
                 if (blockIdx.x == 0 && ok)

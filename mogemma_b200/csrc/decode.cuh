@@ -60,7 +60,7 @@ struct DecodeParams {
     int32_t ids_ld;
     int32_t max_inflight;  // weight/KV tiles a CTA keeps in flight (<= S); bounds memory-queue latency
     int32_t pf_tiles;      // how far (tiles) the producer prefetches into L2 ahead of its ring loads
-    int32_t pad2_;
+    float inv_h;        // 1 / H
 
     const LayerPtrs *layers;
     const void *lm_head;   // [V][Hp]
@@ -94,9 +94,11 @@ struct DecodeParams {
     uint32_t *sync;   // phase counters [n_phases], att_done [L], att_cnt [B*Hkv], exit [1]
     uint32_t *err;    // device error word
     int32_t n_phases;
-    int32_t pad1_;
+    float inv_hd;       // 1 / head_dim
     // optional timeline: [G][n_phases][kTraceSlots] %globaltimer stamps, then [G][2] kernel begin/end
     uint64_t *trace;
+    float att_scale;    // 1 / sqrt(head_dim), as the reference computes it (layers.mojo:65)
+    float emb_scale;    // sqrt(H) (layers.mojo:247-251)
 };
 
 // trace slots per (CTA, phase)

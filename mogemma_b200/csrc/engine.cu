@@ -534,6 +534,10 @@ static DecodeParams base_params(mg_model *m, int B) {
     p.Hkv = m->Hkv;
     p.hd = m->hd;
     p.hdp = m->hdp;
+    p.inv_h = 1.0f / static_cast<float>(m->H);
+    p.inv_hd = 1.0f / static_cast<float>(m->hd);
+    p.att_scale = 1.0f / sqrtf(static_cast<float>(m->hd));
+    p.emb_scale = sqrtf(static_cast<float>(m->H));
     p.I = m->I;
     p.Ip = m->Ip;
     p.V = m->V;
