@@ -104,6 +104,13 @@ def algorithmic_bytes(info, pos0: int, n: int) -> float:
     return float(info.weight_bytes_per_step + kv_read + kv_write + logits + emb_row)
 
 
+# DRAM bytes (read + write) per decode launch over its algorithmic bytes, from
+# one ncu capture of this kernel on the Gemma3-270M shape (the full Gemma3-1B
+# workload is too large to capture): profiles/decode_kernel_gemma3-270m_full.md.
+# Traffic is almost all weight reads, so it scales with the algorithmic bytes.
+TRAFFIC_RATIO = {("gemma3-1b", "f32"): 1.0036, ("gemma3-270m", "f32"): 1.0036}
+
+
 def cpu_baseline(weights: dict, threads: int, n_tokens: int) -> dict:
     """Oracle port on the host: n_tokens decode steps from an empty cache."""
     sys.path.insert(0, str(ROOT / "oracle"))
@@ -305,7 +312,10 @@ def main() -> None:
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * DECODE,
                     "d2h_bytes_per_step": 4 * DECODE},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                         "frac": achieved / pk["hbm_gbs"],
+                         "traffic": (bytes_launch * TRAFFIC_RATIO[(CONFIG, args.weight_dtype)]
+                                     if (CONFIG, args.weight_dtype) in TRAFFIC_RATIO else None),
+                         "traffic_source": "ncu dram__bytes_read+write of a Gemma3-270M launch, scaled by bytes",
                          "peak_source": pk["source"], "kernel": "decode_kernel (one launch per token)",
                          "algorithmic_bytes_per_launch": bytes_launch},
             "cpu_baseline": cpu,
