@@ -98,6 +98,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0u;
 }
+// Same, but the thread may sleep up to `ns` nanoseconds inside the instruction
+// until the phase completes: a waiting warp then takes no issue slots from the
+// warps that share its SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0u;
+}
 // Non-blocking probe of a phase.
 __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
@@ -110,13 +124,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0u;
 }
+constexpr uint32_t kMbarSleepNs = 20000;  // longest sleep per poll; a completed phase wakes the thread
 // Bounded wait for the phase with `parity` to complete.  The error word and
 // the clock are consulted only every 32 polls, keeping the hot poll local.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t n = 1;; ++n) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, kMbarSleepNs)) return true;
         if ((n & 31u) == 0u) {
             if (ld_relaxed_u32(err) != 0u) return false;
             if (globaltimer_ns() - t0 > kWaitBudgetNs) {

@@ -1,0 +1,1238 @@
+// decode_kernel.cuh -- persistent sm_100a decode kernel for the Gemma 3 forward step.
+//
+// Restates, for B rows at once, forward_step (src/mo/mogemma/layers.mojo:224-288)
+// with forward_layer (174-220), forward_attention (16-97) and forward_mlp
+// (101-118), plus the token draw of _sample_next_token (src/py/mogemma/model.py:
+// 103-150).  Layout and scheduling are this library's own:
+//
+//  * Every projection is a GEMV phase whose rows are split evenly over the CTAs
+//    (one CTA per SM).  Weight rows are padded to 128 elements on the device.
+//  * Warp 8 of each CTA is a producer: one lane walks the CTA's tile schedule
+//    for the whole launch and streams weight tiles (and cached K/V rows for
+//    attention) into a ring of shared-memory stages with cp.async.bulk, ahead
+//    of the consumers and across phase boundaries (weights never depend on
+//    activations).
+//  * Warps 0-7 consume: each phase waits on a gpu-scope counter for its input
+//    activations, builds the normalised input vector in shared memory (RMSNorm
+//    with (1 + w), residual adds), then multiplies it by the staged tiles with
+//    128-bit shared loads and warp-shuffle reductions.  Norm weights and RoPE
+//    rows are loaded before the wait so one L2 round trip follows it.
+//  * Fusions: input/pre-ff/post-attn/post-ff/final norms and residual adds in
+//    the next phase's prologue; QK-norm, RoPE and the K/V write in the attention
+//    prologue; GeGLU in the gate/up epilogue; the split-KV combine in the
+//    o_proj prologue; a per-CTA top-k of the lm_head rows in its epilogue; the
+//    draw in the last phase.
+//  * All waits are bounded (common.cuh); on timeout the kernel fast-forwards.
+//  * The batch row count NB is a template parameter of the whole kernel: a
+//    launch for B rows runs code sized for exactly B rows.  Loops over rows
+//    sized for the largest batch cost the batch-1 decode about 2.5 us per norm
+//    prologue (measured), so each row count is its own instantiation, compiled
+//    in its own translation unit (decode_nb<N>.cu).
+#pragma once
+#include "common.cuh"
+#include "decode.cuh"
+#include "select.cuh"
+
+namespace mg {
+
+// ---------------------------------------------------------------- sync layout
+__device__ __forceinline__ uint32_t *ctr_phase(const DecodeParams &p, int ph) { return p.sync + ph; }
+__device__ __forceinline__ uint32_t *ctr_exit(const DecodeParams &p) { return p.sync + p.n_phases; }
+
+__device__ __forceinline__ void phase_of(int ph, int L, int &kind, int &layer) {
+    if (ph < 5 * L) {
+        layer = ph / 5;
+        kind = ph - 5 * layer;
+    } else if (ph == 5 * L) {
+        kind = PH_LMH;
+        layer = L - 1;
+    } else {
+        kind = PH_SAMPLE;
+        layer = L - 1;
+    }
+}
+
+// Rotating slot so the CTAs that get one extra row differ from phase to phase.
+__device__ __forceinline__ int cta_slot(int ph) { return static_cast<int>((blockIdx.x + 61u * ph) % gridDim.x); }
+
+template <typename WT>
+struct GemvGeom {
+    const WT *tiles;  // this CTA's first tile (tiled layout, see tile_shape)
+    bool pair;        // gate/up phase: each tile holds gate rows then up rows
+    int64_t row0;     // first output row of this CTA
+    int nrows;        // output rows of this CTA (the last group may be partial)
+    int Kp, kc, nseg, rps, ngroups;
+    int tile_elems;
+};
+
+template <typename WT>
+__device__ __forceinline__ void gemv_geom(const DecodeParams &p, const LayerPtrs &lp, int kind, int ph,
+                                          GemvGeom<WT> &g) {
+    int N;
+    const WT *base;
+    g.pair = false;
+    switch (kind) {
+        case PH_QKV:
+            N = p.qkv_rows;
+            g.Kp = p.Hp;
+            base = static_cast<const WT *>(lp.qkv);
+            break;
+        case PH_O:
+            N = p.H;
+            g.Kp = p.Ap;
+            base = static_cast<const WT *>(lp.o);
+            break;
+        case PH_GU:
+            N = p.I;
+            g.Kp = p.Hp;
+            base = static_cast<const WT *>(lp.gate);
+            g.pair = true;
+            break;
+        case PH_D:
+            N = p.H;
+            g.Kp = p.Ip;
+            base = static_cast<const WT *>(lp.down);
+            break;
+        default:
+            N = (p.lm_mode == kLmLogits) ? p.V : 0;
+            g.Kp = p.Hp;
+            base = static_cast<const WT *>(p.lm_head);
+            break;
+    }
+    const TileShape ts = tile_shape(g.Kp, static_cast<int>(sizeof(WT)), g.pair);
+    g.rps = ts.rps;
+    g.kc = ts.kc;
+    g.nseg = ts.nseg;
+    g.tile_elems = static_cast<int>(tile_elems(ts));
+    // row groups are split evenly over the CTAs, rotating the remainder by phase
+    const int groups = (N + g.rps - 1) / g.rps;
+    const int slot = cta_slot(ph);
+    const int g0 = static_cast<int>(static_cast<int64_t>(groups) * slot / gridDim.x);
+    const int g1 = static_cast<int>(static_cast<int64_t>(groups) * (slot + 1) / gridDim.x);
+    g.ngroups = g1 - g0;
+    g.row0 = static_cast<int64_t>(g0) * g.rps;
+    g.nrows = static_cast<int>(min(static_cast<int64_t>(N), static_cast<int64_t>(g1) * g.rps) - g.row0);
+    if (g.nrows < 0) g.nrows = 0;
+    g.tiles = base + static_cast<int64_t>(g0) * g.nseg * g.tile_elems;
+}
+
+// Attention work split: items are (row, kv head, chunk of att_ch positions).
+struct AttRows {
+    int lo[kMaxRows], nch[kMaxRows];
+    int nitems;
+};
+
+template <int NB>
+__device__ __forceinline__ void att_rows(const DecodeParams &p, bool global, const int *s_pos, AttRows &a) {
+    a.nitems = 0;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        {
+            const int pos = s_pos[b];
+            int lo = 0;
+            if (!global && p.window > 0 && pos - p.window + 1 > 0) lo = pos - p.window + 1;
+            a.lo[b] = lo;
+            a.nch[b] = (pos + 1 - lo + p.att_ch - 1) / p.att_ch;
+            a.nitems += p.Hkv * a.nch[b];
+        }
+    }
+}
+
+__device__ __forceinline__ void att_item(const DecodeParams &p, const AttRows &a, int item, int &b, int &kvh,
+                                         int &c) {
+    int base = 0;
+    b = 0;
+    for (; b < p.B - 1; ++b) {
+        const int cnt = p.Hkv * a.nch[b];
+        if (item < base + cnt) break;
+        base += cnt;
+    }
+    const int r = item - base;
+    kvh = r / a.nch[b];
+    c = r - kvh * a.nch[b];
+}
+
+__device__ __forceinline__ float *att_part(const DecodeParams &p, int b, int kvh, int c) {
+    const int Gq = p.Hq / p.Hkv;
+    return p.attn_part + ((static_cast<int64_t>(b) * p.Hkv + kvh) * kMaxChunks + c) * Gq * (p.hd + 2);
+}
+
+// ---------------------------------------------------------------- shared memory
+struct Smem {
+    uint64_t *full;
+    uint64_t *empty;
+    unsigned char *ring;
+    float *xs;  // activation stage / attention scratch / selection scratch
+    LayerPtrs *layers;
+};
+
+struct SmallSmem {
+    AttRows att;    // consumers' split of the current attention phase
+    AttRows att_p;  // the producer's (it runs phases ahead)
+    int pos[kMaxRows];
+    int tok[kMaxRows];
+    int active[kMaxRows];
+    float red[kConsumerWarps * kMaxRows];
+    uint32_t flag;
+    uint32_t pad_;
+    uint64_t *tr_ready;  // trace slots of the current phase (consumer thread 0 only)
+    uint64_t *tr_end;
+};
+
+// Optional timeline stamp (see kTraceSlots); null trace pointer = off.
+__device__ __forceinline__ uint64_t *trace_slot(const DecodeParams &p, int ph, int slot) {
+    return p.trace ? p.trace + (static_cast<size_t>(blockIdx.x) * p.n_phases + ph) * kTraceSlots + slot : nullptr;
+}
+__device__ __forceinline__ void trace_mark(uint64_t *slot) {
+    if (slot) *slot = globaltimer_ns();
+}
+
+// ---------------------------------------------------------------- consumer helpers
+// Sum over the consumer threads of each of NB per-thread row values.
+template <int NB>
+__device__ __forceinline__ void block_sum_rows(float (&v)[NB], SmallSmem &ss, int tid) {
+    const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        const float s = warp_sum(v[b]);
+        if (lane == 0) ss.red[warp * kMaxRows + b] = s;
+    }
+    consumer_sync(kConsumerThreads);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) t += ss.red[w * kMaxRows + b];
+        v[b] = t;
+    }
+    consumer_sync(kConsumerThreads);
+}
+
+constexpr int kNormPer = 8;  // elements per thread held in registers per chunk (H <= 2048 in one chunk)
+
+// Norm weights of a phase prologue, loaded before its dependency wait.
+struct NormW {
+    float wa[kNormPer], wn[kNormPer];
+};
+__device__ __forceinline__ void norm_prefetch(NormW &nw, const float *w_add, const float *w_next, int H, int tid) {
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) {
+        const int i = tid + j * kConsumerThreads;
+        nw.wa[j] = (w_add != nullptr && i < H) ? __ldg(w_add + i) : 0.f;
+        nw.wn[j] = (w_next != nullptr && i < H) ? __ldg(w_next + i) : 0.f;
+    }
+    // Pin the loads here: without this the compiler may sink them past the
+    // dependency wait, onto the prologue's critical path.
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) asm volatile("" : "+f"(nw.wa[j]), "+f"(nw.wn[j]));
+}
+
+// For rows b < NB:  x = base[b] + rmsnorm(add[b]) * (1 + w_add);  out[b] <- x
+// (when out != null);  xs[b] <- rmsnorm(x) * (1 + w_next), zero padded to Kp.
+// base/add rows ([NB][H] in global memory) were written by other CTAs and are
+// read through L2; all loads of a chunk are issued before any is used.
+template <int NB>
+__device__ __forceinline__ void stage_norm(const float *base, const float *add, const float *w_add,
+                                           const float *w_next, const NormW &nw, float *out, int H, float inv_h,
+                                           int Kp, float *xs, SmallSmem &ss, int tid) {
+    float sq[NB], sq2[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) sq[b] = sq2[b] = 0.f;
+    float *xb = xs + NB * Kp;  // base rows staged next to the activation stage
+    for (int j0 = 0; j0 * kConsumerThreads < H; j0 += kNormPer) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            float v[kNormPer], bv[kNormPer];
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) {
+                const int i = tid + (j0 + j) * kConsumerThreads;
+                v[j] = i < H ? __ldcg(add + static_cast<int64_t>(b) * H + i) : 0.f;
+                bv[j] = i < H ? __ldcg(base + static_cast<int64_t>(b) * H + i) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) {
+                const int i = tid + (j0 + j) * kConsumerThreads;
+                if (i < H) {
+                    xs[b * Kp + i] = v[j];
+                    xb[b * H + i] = bv[j];
+                }
+                sq[b] += v[j] * v[j];
+            }
+        }
+    }
+    block_sum_rows<NB>(sq, ss, tid);
+    // The first chunk uses the prefetched weights; later chunks (H > 2048) load
+    // theirs.  Separate branches keep the first chunk free of global loads.
+    for (int j0 = 0; j0 * kConsumerThreads < H; j0 += kNormPer) {
+        float wa[kNormPer];
+        if (j0 == 0) {
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) wa[j] = nw.wa[j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) {
+                const int i = tid + (j0 + j) * kConsumerThreads;
+                wa[j] = i < H ? __ldg(w_add + i) : 0.f;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float inv = rms_inv(sq[b], inv_h);
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) {
+                const int i = tid + (j0 + j) * kConsumerThreads;
+                if (i < H) {
+                    const float x = xb[b * H + i] + xs[b * Kp + i] * inv * (1.0f + wa[j]);
+                    xs[b * Kp + i] = x;
+                    if (out) out[static_cast<int64_t>(b) * H + i] = x;
+                    sq2[b] += x * x;
+                }
+            }
+        }
+    }
+    block_sum_rows<NB>(sq2, ss, tid);
+    for (int j0 = 0; j0 * kConsumerThreads < Kp; j0 += kNormPer) {
+        float wn[kNormPer];
+        if (j0 == 0) {
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) wn[j] = nw.wn[j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) {
+                const int i = tid + (j0 + j) * kConsumerThreads;
+                wn[j] = i < H ? __ldg(w_next + i) : 0.f;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float inv = rms_inv(sq2[b], inv_h);
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) {
+                const int i = tid + (j0 + j) * kConsumerThreads;
+                if (i < Kp) xs[b * Kp + i] = i < H ? xs[b * Kp + i] * inv * (1.0f + wn[j]) : 0.0f;
+            }
+        }
+    }
+    consumer_sync(kConsumerThreads);
+}
+
+// Layer 0 input: x = E[tok] * sqrt(H) (model.mojo:62-68, layers.mojo:247-251),
+// out <- x, xs <- rmsnorm(x) * (1 + w).
+template <typename WT, int NB>
+__device__ __noinline__ void stage_embed(const WT *E, int64_t ld, const int *toks, const float *w, float *out,
+                                         int H, float inv_h, float scale, int Kp, float *xs, SmallSmem &ss,
+                                         int tid) {
+    float sq[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        float s = 0.f;
+        for (int i = tid; i < H; i += kConsumerThreads) {
+            const float x = ld_w(E + static_cast<int64_t>(toks[b]) * ld + i) * scale;
+            xs[b * Kp + i] = x;
+            if (out) out[static_cast<int64_t>(b) * H + i] = x;
+            s += x * x;
+        }
+        sq[b] = s;
+    }
+    block_sum_rows<NB>(sq, ss, tid);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        const float inv = rms_inv(sq[b], inv_h);
+        for (int i = tid; i < Kp; i += kConsumerThreads) xs[b * Kp + i] = i < H ? xs[b * Kp + i] * inv * (1.0f + w[i]) : 0.f;
+    }
+    consumer_sync(kConsumerThreads);
+}
+
+// Announce this CTA's part of a phase (release at gpu scope).
+__device__ __forceinline__ void cta_signal(uint32_t *ctr, uint32_t n, SmallSmem &ss, int tid) {
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) {
+        // The barrier orders every consumer's writes before thread 0's release;
+        // red.release is cumulative over them at gpu scope.
+        if (n) red_release_add_u32(ctr, n);
+        trace_mark(ss.tr_end);
+    }
+}
+
+// Wait for a counter; uniform result across consumer threads.
+__device__ __forceinline__ bool cta_wait(const uint32_t *ctr, uint32_t target, uint32_t *err, uint32_t site,
+                                         SmallSmem &ss, int tid) {
+    if (tid == 0) {
+        ss.flag = wait_counter_geq(ctr, target, err, site) ? 1u : 0u;
+        trace_mark(ss.tr_ready);
+    }
+    consumer_sync(kConsumerThreads);
+    const bool ok = ss.flag != 0u;
+    consumer_sync(kConsumerThreads);
+    return ok;
+}
+
+// ---------------------------------------------------------------- GEMV consumer
+// Where a GEMV phase's row results go: out[b * ld + row] = dot, or with a
+// gate/up pair out[b * ld + row] = gelu_erf(gate) * up (ops.mojo:19-22).
+struct GemvOut {
+    float *out;
+    int64_t ld;
+};
+
+// NB (rows of x) and PAIR (gate/up) are compile-time so the inner loop is a
+// straight run of 128-bit shared loads and FMAs with accumulators in
+// registers.
+template <typename WT, int NB, bool PAIR>
+__device__ __forceinline__ void gemv_tiles(const GemvGeom<WT> &g, const float *__restrict__ xs, const Smem &sm, int S,
+                                        uint32_t &tile, uint32_t *err, bool &ok, int tid, uint64_t *tr_first,
+                                        GemvOut o) {
+    constexpr int rpw = sizeof(WT) == 2 ? 2 : 1;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int Kp = g.Kp;
+    for (int grp = 0; grp < g.ngroups; ++grp) {
+        const int nr = min(g.rps, g.nrows - grp * g.rps);
+        float acc[rpw][NB], acc2[rpw][NB];
+#pragma unroll
+        for (int k = 0; k < rpw; ++k)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) acc[k][b] = acc2[k][b] = 0.f;
+        for (int s = 0; s < g.nseg; ++s, ++tile) {
+            const int st = static_cast<int>(tile % S);
+            const uint32_t par = (tile / S) & 1u;
+            if (ok) ok = mbar_wait(&sm.full[st], par, err, kErrTimeoutFull | 1u);
+            if (grp == 0 && s == 0 && tid == 0) trace_mark(tr_first);
+            const int c0 = s * g.kc;
+            const int sw = min(g.kc, Kp - c0);
+            const WT *stage = reinterpret_cast<const WT *>(sm.ring + static_cast<size_t>(st) * kStageBytes);
+            const float *xseg = xs + c0;
+            if (ok && warp * rpw < nr) {
+                const WT *wr = stage + static_cast<size_t>(warp * rpw) * g.kc;
+#pragma unroll 2
+                for (int c = lane * 4; c < sw; c += 128) {
+                    float4 x4[NB];
+#pragma unroll
+                    for (int b = 0; b < NB; ++b) x4[b] = *reinterpret_cast<const float4 *>(xseg + b * Kp + c);
+#pragma unroll
+                    for (int k = 0; k < rpw; ++k) {
+                        const float4 w4 = lds_w4(wr + k * g.kc + c);
+#pragma unroll
+                        for (int b = 0; b < NB; ++b)
+                            acc[k][b] += w4.x * x4[b].x + w4.y * x4[b].y + w4.z * x4[b].z + w4.w * x4[b].w;
+                        if constexpr (PAIR) {
+                            const float4 u4 = lds_w4(wr + (g.rps + k) * g.kc + c);
+#pragma unroll
+                            for (int b = 0; b < NB; ++b)
+                                acc2[k][b] += u4.x * x4[b].x + u4.y * x4[b].y + u4.z * x4[b].z + u4.w * x4[b].w;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[st]);
+        }
+#pragma unroll
+        for (int k = 0; k < rpw; ++k) {
+            const int j = warp * rpw + k;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                const float d = warp_sum(acc[k][b]);
+                if constexpr (PAIR) {
+                    const float u = warp_sum(acc2[k][b]);
+                    if (lane == 0 && j < nr && ok) {
+                        const float gelu = 0.5f * d * (1.0f + erff(d * kInvSqrt2));
+                        o.out[b * o.ld + g.row0 + grp * g.rps + j] = gelu * u;
+                    }
+                } else {
+                    if (lane == 0 && j < nr && ok) o.out[b * o.ld + g.row0 + grp * g.rps + j] = d;
+                }
+            }
+        }
+    }
+}
+
+template <typename WT, int NB>
+__device__ __forceinline__ void gemv_consume(const GemvGeom<WT> &g, const float *xs, const Smem &sm, int S,
+                                             uint32_t &tile, uint32_t *err, bool &ok, int tid, uint64_t *tr_first,
+                                             GemvOut o) {
+    if (g.pair)
+        gemv_tiles<WT, NB, true>(g, xs, sm, S, tile, err, ok, tid, tr_first, o);
+    else
+        gemv_tiles<WT, NB, false>(g, xs, sm, S, tile, err, ok, tid, tr_first, o);
+}
+
+// ---------------------------------------------------------------- attention
+// Split-KV attention for this CTA's items of one layer (layers.mojo:16-97):
+// QK-norm + RoPE of the group's q heads and the new k, K/V write at pos,
+// online-softmax over the chunk's cached positions (staged by the producer),
+// partial (m, l, acc) per (row, kv head, chunk).  Returns the item count.
+// HD (head dim) and GQ (q heads per kv head) are compile-time when non-zero so
+// every loop unrolls and its shared/global loads issue together.
+// Result of a CTA's attention items: partials written, and the consumer's
+// ring position and status afterwards (returned by value so that nothing of
+// the caller has to live in local memory across the call).
+struct AttRet {
+    uint32_t done, tile;
+    bool ok;
+};
+
+template <int HD, int GQ>
+__device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, SmallSmem &ss, const LayerPtrs &lp,
+                                         int layer, int ph, const AttRows &a, uint32_t tile, bool ok, int tid,
+                                         bool has_dep) {
+    constexpr int kQ = GQ ? GQ : kMaxQPerKv;         // accumulator slots
+    constexpr int kDL = HD ? HD / 32 : kMaxHeadDim / 32;  // head dims per lane
+    const int G = gridDim.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int Gq = GQ ? GQ : p.Hq / p.Hkv;
+    const int hd = HD ? HD : p.hd;
+    const int half = hd / 2;
+    const int B = p.B;
+    const int hdp = HD ? HD : p.hdp;
+    // shared scratch: q [Gq][hd], k, v, scores [Gq][kAttTile], m/l/alpha, norm weights, rope rows [B][hd]
+    float *q_s = sm.xs;
+    float *k_s = q_s + Gq * hd;
+    float *v_s = k_s + hd;
+    float *sc = v_s + hd;
+    float *m_s = sc + Gq * kAttTile;
+    float *l_s = m_s + kMaxQPerKv;
+    float *al_s = l_s + kMaxQPerKv;
+    float *qn_s = al_s + kMaxQPerKv;
+    float *kn_s = qn_s + hd;
+    float *rope_s = kn_s + hd;  // [B][half cos | half sin]
+    // independent of the QKV results: norm weights and this step's RoPE rows
+    {
+        const float *ct = lp.is_global ? p.rope_cos_g : p.rope_cos_l;
+        const float *st_ = lp.is_global ? p.rope_sin_g : p.rope_sin_l;
+        for (int i = tid; i < hd; i += kConsumerThreads) {
+            qn_s[i] = lp.q_norm ? lp.q_norm[i] : 0.f;
+            kn_s[i] = lp.k_norm ? lp.k_norm[i] : 0.f;
+        }
+        for (int i = tid; i < B * half; i += kConsumerThreads) {
+            const int b = i / half, d = i - b * half;
+            rope_s[b * hd + d] = ct[static_cast<int64_t>(ss.pos[b]) * half + d];
+            rope_s[b * hd + half + d] = st_[static_cast<int64_t>(ss.pos[b]) * half + d];
+        }
+    }
+    if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+    const float scale = p.att_scale;
+    const int slot = cta_slot(ph);
+    uint32_t done = 0;
+    for (int item = slot; item < a.nitems; item += G) {
+        int b, kvh, c;
+        att_item(p, a, item, b, kvh, c);
+        const int pos = ss.pos[b];
+        const int t_begin = a.lo[b] + c * p.att_ch;
+        const int t_end = min(t_begin + p.att_ch, pos + 1);
+        // ---- raw q (Gq heads), k, v of this kv group: all loads in one round trip
+        {
+            const float *qkv_b = p.qkv + static_cast<int64_t>(b) * p.qkv_rows;
+            constexpr int kPer = (kMaxQPerKv + 2) * kMaxHeadDim / kConsumerThreads;
+            const int n = (Gq + 2) * hd;
+            float v[kPer];
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int i = tid + j * kConsumerThreads;
+                int64_t src = 0;
+                if (i < n) {
+                    const int vec = i / hd, d = i - vec * hd;
+                    src = vec < Gq ? static_cast<int64_t>(kvh * Gq + vec) * hd + d
+                                   : p.A + static_cast<int64_t>((vec == Gq ? 0 : p.Hkv) + kvh) * hd + d;
+                }
+                v[j] = i < n ? __ldcg(qkv_b + src) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int i = tid + j * kConsumerThreads;
+                if (i < n) q_s[i] = v[j];  // q_s, k_s, v_s are contiguous
+            }
+        }
+        if (tid < Gq) {
+            m_s[tid] = -INFINITY;
+            l_s[tid] = 0.f;
+        }
+        consumer_sync(kConsumerThreads);
+        if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttLoaded));
+        // ---- QK-norm (layers.mojo:43-49) and RoPE (52-55), one warp per vector
+        for (int vec = warp; vec < Gq + 1; vec += kConsumerWarps) {
+            float *x = q_s + vec * hd;
+            const bool has_norm = vec < Gq ? lp.q_norm != nullptr : lp.k_norm != nullptr;
+            const float *nwt = vec < Gq ? qn_s : kn_s;
+            if (has_norm) {
+                float s = 0.f;
+#pragma unroll
+                for (int i = 0; i < kDL; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < hd) s += x[d] * x[d];
+                }
+                s = warp_sum(s);
+                const float inv = rms_inv(s, p.inv_hd);
+#pragma unroll
+                for (int i = 0; i < kDL; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < hd) x[d] = x[d] * inv * (1.0f + nwt[d]);
+                }
+                __syncwarp();
+            }
+            const float *cs = rope_s + b * hd;
+#pragma unroll
+            for (int i0 = 0; i0 < (kDL + 1) / 2; ++i0) {
+                const int i = lane + 32 * i0;
+                if (i < half) {
+                    const float x1 = x[i], x2 = x[i + half];
+                    x[i] = x1 * cs[i] - x2 * cs[half + i];
+                    x[i + half] = x2 * cs[i] + x1 * cs[half + i];
+                }
+            }
+            __syncwarp();
+        }
+        consumer_sync(kConsumerThreads);
+        if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttRoped));
+        // ---- K/V write at pos by the chunk that ends there (layers.mojo:57-61)
+        if (t_end == pos + 1 && ss.active[b] && ok) {
+            const size_t off = static_cast<size_t>(layer) * p.kv_layer_stride + static_cast<size_t>(b) * p.kv_row_stride +
+                               static_cast<size_t>(kvh) * p.kv_head_stride + static_cast<size_t>(pos) * hdp;
+            for (int d = tid; d < hd; d += kConsumerThreads) {
+                p.kc[off + d] = k_s[d];
+                p.vc[off + d] = v_s[d];
+            }
+        }
+        // P.V ownership: thread -> head dim pv_d, position class pv_q of ntq
+        const int ntq = kConsumerThreads / hd;
+        const int pv_d = tid % hd, pv_q = tid / hd;
+        const bool pv_on = pv_q < ntq;
+        float acc[kQ];
+#pragma unroll
+        for (int h = 0; h < kQ; ++h) acc[h] = 0.f;
+        for (int ts = t_begin; ts < t_end; ts += kAttTile, ++tile) {
+            const int st = static_cast<int>(tile % p.S);
+            if (ok) ok = mbar_wait(&sm.full[st], (tile / p.S) & 1u, p.err, kErrTimeoutFull | 2u);
+            if (tid == 0 && done == 0 && ts == t_begin) trace_mark(trace_slot(p, ph, kTrPrologue));
+            const int nt = min(kAttTile, t_end - ts);
+            const float *kt = reinterpret_cast<const float *>(sm.ring + static_cast<size_t>(st) * kStageBytes);
+            const float *vt = kt + kAttTile * hdp;
+            // scores s = (q . k) * scale (layers.mojo:74-79): warp w takes positions w and w + 8,
+            // lanes run over head dims, every q head accumulates at once
+            {
+                const int t0 = warp, t1 = warp + kConsumerWarps;
+                const bool v0 = t0 < nt, v1 = t1 < nt;
+                const float *k0 = (ts + t0 == pos) ? k_s : kt + t0 * hdp;
+                const float *k1 = (ts + t1 == pos) ? k_s : kt + t1 * hdp;
+                float s0[kQ], s1[kQ];
+#pragma unroll
+                for (int h = 0; h < kQ; ++h) s0[h] = s1[h] = 0.f;
+#pragma unroll
+                for (int i = 0; i < kDL; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < hd) {
+                        const float ka = v0 ? k0[d] : 0.f;
+                        const float kb = v1 ? k1[d] : 0.f;
+#pragma unroll
+                        for (int h = 0; h < kQ; ++h) {
+                            if (h < Gq) {
+                                const float q = q_s[h * hd + d];
+                                s0[h] += q * ka;
+                                s1[h] += q * kb;
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < kQ; ++h) {
+                    if (h < Gq) {
+                        const float a0 = warp_sum(s0[h]);
+                        const float a1 = warp_sum(s1[h]);
+                        if (lane == 0) {
+                            if (v0) sc[h * kAttTile + t0] = a0 * scale;
+                            if (v1) sc[h * kAttTile + t1] = a1 * scale;
+                        }
+                    }
+                }
+            }
+            consumer_sync(kConsumerThreads);
+            // online softmax bookkeeping, one warp per head
+            for (int h = warp; h < Gq; h += kConsumerWarps) {
+                const float s = lane < nt ? sc[h * kAttTile + lane] : -INFINITY;
+                const float mx = warp_max(s);
+                const float m_old = m_s[h];
+                const float m_new = fmaxf(m_old, mx);
+                const float e = lane < nt ? expf(s - m_new) : 0.f;
+                if (lane < nt) sc[h * kAttTile + lane] = e;
+                const float es = warp_sum(e);
+                if (lane == 0) {
+                    const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+                    al_s[h] = alpha;
+                    l_s[h] = l_s[h] * alpha + es;
+                    m_s[h] = m_new;
+                }
+            }
+            consumer_sync(kConsumerThreads);
+            // P @ V (layers.mojo:89-94): Gq independent accumulators per thread
+            if (pv_on) {
+#pragma unroll
+                for (int h = 0; h < kQ; ++h)
+                    if (h < Gq) acc[h] *= al_s[h];
+#pragma unroll 4
+                for (int t = pv_q; t < nt; t += ntq) {
+                    const float vv = (ts + t == pos) ? v_s[pv_d] : vt[t * hdp + pv_d];
+#pragma unroll
+                    for (int h = 0; h < kQ; ++h)
+                        if (h < Gq) acc[h] += sc[h * kAttTile + t] * vv;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[st]);
+            consumer_sync(kConsumerThreads);
+        }
+        if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttTiles));
+        // ---- partial (m, l, acc) of this chunk; combined in the o_proj prologue
+        float *part = att_part(p, b, kvh, c);
+        const int part_ld = hd + 2;
+        if (ntq > 1) {  // fold the position classes
+            float *red = rope_s + B * hd;  // [ntq][Gq][hd]
+            if (pv_on)
+#pragma unroll
+                for (int h = 0; h < kQ; ++h)
+                    if (h < Gq) red[(pv_q * Gq + h) * hd + pv_d] = acc[h];
+            consumer_sync(kConsumerThreads);
+            if (pv_q == 0) {
+#pragma unroll
+                for (int h = 0; h < kQ; ++h) {
+                    if (h < Gq) {
+                        float s = 0.f;
+                        for (int q = 0; q < ntq; ++q) s += red[(q * Gq + h) * hd + pv_d];
+                        acc[h] = s;
+                    }
+                }
+            }
+        }
+        if (pv_q == 0) {
+#pragma unroll
+            for (int h = 0; h < kQ; ++h)
+                if (h < Gq) part[h * part_ld + 2 + pv_d] = acc[h];
+        }
+        if (tid < Gq) {
+            part[tid * part_ld + 0] = m_s[tid];
+            part[tid * part_ld + 1] = l_s[tid];
+        }
+        consumer_sync(kConsumerThreads);
+        if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttPart));
+        ++done;
+    }
+    return AttRet{done, tile, ok};
+}
+
+__device__ __forceinline__ AttRet att_dispatch(const DecodeParams &p, const Smem &sm, SmallSmem &ss,
+                                               const LayerPtrs &lp, int layer, int ph, const AttRows &a,
+                                               uint32_t tile, bool ok, int tid, bool has_dep) {
+    const int Gq = p.Hq / p.Hkv;
+#define MG_ATT(HD_, GQ_) \
+    if (p.hd == HD_ && Gq == GQ_) return att_items<HD_, GQ_>(p, sm, ss, lp, layer, ph, a, tile, ok, tid, has_dep);
+    MG_ATT(256, 4)
+    MG_ATT(256, 3)
+    MG_ATT(256, 2)
+    MG_ATT(256, 1)
+    MG_ATT(128, 2)
+    MG_ATT(128, 4)
+    MG_ATT(64, 4)
+#undef MG_ATT
+    return att_items<0, 0>(p, sm, ss, lp, layer, ph, a, tile, ok, tid, has_dep);
+}
+
+// o_proj input from the split-KV partials of every (row, kv head):
+//   w_c = exp(m_c - M) / sum_c l_c exp(m_c - M);  x[b][h*hd+d] = sum_c w_c * acc_c[d]
+// One warp per (row, q head): lanes hold one chunk's weight, then run over
+// head dims with eight chunks of loads in flight.
+static __device__ __noinline__ void att_combine(const DecodeParams &p, const AttRows &a, int Kp, float *xs, int tid) {
+    const int lane = tid & 31, warp = tid >> 5;
+    const int Gq = p.Hq / p.Hkv, hd = p.hd, B = p.B;
+    const int part_ld = hd + 2;
+    const int64_t cstride = static_cast<int64_t>(Gq) * part_ld;
+    constexpr int kDims = kMaxHeadDim / 32;
+    constexpr int kCh = 8;
+    for (int bh = warp; bh < B * p.Hq; bh += kConsumerWarps) {
+        const int b = bh / p.Hq, hq = bh - b * p.Hq;
+        const int kvh = hq / Gq, hl = hq - kvh * Gq;
+        const int nch = a.nch[b];
+        const float *base = att_part(p, b, kvh, 0) + hl * part_ld;
+        float m = -INFINITY, l = 0.f;
+        if (lane < nch) {
+            m = __ldcg(base + lane * cstride);
+            l = __ldcg(base + lane * cstride + 1);
+        }
+        const float M = warp_max(m);
+        const float e = lane < nch ? expf(m - M) : 0.f;
+        const float w = e / warp_sum(l * e);
+        float x[kDims];
+#pragma unroll
+        for (int i = 0; i < kDims; ++i) x[i] = 0.f;
+        for (int c0 = 0; c0 < nch; c0 += kCh) {
+            float v[kCh][kDims];
+#pragma unroll
+            for (int u = 0; u < kCh; ++u)
+#pragma unroll
+                for (int i = 0; i < kDims; ++i) {
+                    const int d = lane + 32 * i;
+                    v[u][i] = (c0 + u < nch && d < hd) ? __ldcg(base + (c0 + u) * cstride + 2 + d) : 0.f;
+                }
+#pragma unroll
+            for (int u = 0; u < kCh; ++u) {
+                const float wu = __shfl_sync(0xffffffffu, w, (c0 + u) & 31);
+#pragma unroll
+                for (int i = 0; i < kDims; ++i) x[i] += wu * v[u][i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kDims; ++i) {
+            const int d = lane + 32 * i;
+            if (d < hd) xs[b * Kp + hq * hd + d] = x[i];
+        }
+    }
+    for (int o = tid; o < B * Kp; o += kConsumerThreads) {
+        const int b = o / Kp, oo = o - b * Kp;
+        if (oo >= p.A) xs[b * Kp + oo] = 0.f;
+    }
+    consumer_sync(kConsumerThreads);
+}
+
+// Per-CTA top-k of the lm_head rows (keys to cand_key).  The CTA's logits are
+// staged in the (now idle) ring first: one batched read instead of a round
+// trip per radix pass.
+static __device__ __noinline__ void lm_topk(const DecodeParams &p, const Smem &sm, int64_t row0, int nrows, int tid) {
+    const int G = gridDim.x;
+    SelectSmem &sel = *reinterpret_cast<SelectSmem *>(sm.xs);
+    uint64_t *outk = reinterpret_cast<uint64_t *>(reinterpret_cast<unsigned char *>(sm.xs) + sizeof(SelectSmem));
+    float *lg = reinterpret_cast<float *>(sm.ring);  // nrows <= V / G + 1 floats, far below one stage
+    for (int b = 0; b < p.B; ++b) {
+        const float *lr = p.logits + static_cast<int64_t>(b) * p.V + row0;
+        for (int i0 = 0; i0 < nrows; i0 += 8 * kConsumerThreads) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + tid + j * kConsumerThreads;
+                v[j] = i < nrows ? lr[i] : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + tid + j * kConsumerThreads;
+                if (i < nrows) lg[i] = v[j];
+            }
+        }
+        consumer_sync(kConsumerThreads);
+        const uint32_t r0 = static_cast<uint32_t>(row0);
+        block_select_topk(
+            nrows, p.topk, [&](int i) { return topk_key(lg[i], r0 + static_cast<uint32_t>(i)); }, outk, sel, tid,
+            kConsumerThreads, [] { consumer_sync(kConsumerThreads); });
+        uint64_t *dst = p.cand_key + (static_cast<int64_t>(b) * G + blockIdx.x) * kMaxTopK;
+        for (int j = tid; j < p.topk; j += kConsumerThreads) dst[j] = outk[j];
+        consumer_sync(kConsumerThreads);
+    }
+}
+
+// Merge of all CTAs' candidates for row b and the draw (model.py:103-150).
+// Candidates are staged in the idle ring with batched loads first.
+static __device__ __noinline__ int32_t row_draw(const DecodeParams &p, const Smem &sm, int b, bool ok, int tid) {
+    const int G = gridDim.x;
+    SelectSmem &sel = *reinterpret_cast<SelectSmem *>(sm.xs);
+    unsigned char *after = reinterpret_cast<unsigned char *>(sm.xs) + sizeof(SelectSmem);
+    uint64_t *outk = reinterpret_cast<uint64_t *>(after);
+    double *fscr = reinterpret_cast<double *>(after + kMaxTopK * sizeof(uint64_t));
+    int *oscr = reinterpret_cast<int *>(fscr + kMaxTopK);
+    const uint64_t *ck = p.cand_key + static_cast<int64_t>(b) * G * kMaxTopK;
+    const int K = p.topk;
+    const int n = G * K;
+    if (static_cast<size_t>(n) * sizeof(uint64_t) > static_cast<size_t>(p.S) * kStageBytes) {  // ring too small
+        block_select_topk(
+            n, K, [&](int i) { return __ldcg(ck + (i / K) * kMaxTopK + (i % K)); }, outk, sel, tid, kConsumerThreads,
+            [] { consumer_sync(kConsumerThreads); });
+    } else {
+    uint64_t *keys = reinterpret_cast<uint64_t *>(sm.ring);
+    for (int i0 = 0; i0 < n; i0 += 16 * kConsumerThreads) {
+        uint64_t v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int i = i0 + tid + j * kConsumerThreads;
+            v[j] = i < n ? __ldcg(ck + (i / K) * kMaxTopK + (i % K)) : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int i = i0 + tid + j * kConsumerThreads;
+            if (i < n) keys[i] = v[j];
+        }
+    }
+    consumer_sync(kConsumerThreads);
+    block_select_topk(
+        n, K, [&](int i) { return keys[i]; }, outk, sel, tid, kConsumerThreads, [] { consumer_sync(kConsumerThreads); });
+    }
+    int32_t token = -1;
+    if (tid == 0 && ok) {
+        const double u = p.uniforms ? p.uniforms[b] : philox_uniform(p.seed, p.rng_offset, b);
+        token = draw_from_sorted(outk, K, p.temperature, p.top_p, u, fscr, oscr);
+    }
+    return token;
+}
+
+// ---------------------------------------------------------------- consumer phases
+template <typename WT, int NB>
+__device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &ss, int tid) {
+    const int G = gridDim.x;
+    constexpr int B = NB;
+    bool ok = ld_relaxed_u32(p.err) == 0u;
+    uint32_t tile = 0;
+    for (int ph = p.ph_begin; ph < p.ph_end; ++ph) {
+        int kind, layer;
+        phase_of(ph, p.L, kind, layer);
+        const LayerPtrs &lp = sm.layers[layer];
+        const bool has_dep = ph - 1 >= p.ph_begin;
+        if (tid == 0) {
+            trace_mark(trace_slot(p, ph, kTrStart));
+            ss.tr_ready = trace_slot(p, ph, kTrReady);
+            ss.tr_end = trace_slot(p, ph, kTrEnd);
+        }
+        if (kind == PH_QKV) {
+            GemvGeom<WT> g;
+            gemv_geom<WT>(p, lp, kind, ph, g);
+            float *out_h = (blockIdx.x == 0) ? p.h : nullptr;
+            if (layer == 0) {
+                stage_embed<WT, NB>(static_cast<const WT *>(p.embed), p.embed_ld, ss.tok, lp.in_ln, out_h, p.H,
+                                    p.inv_h, p.emb_scale, g.Kp, sm.xs, ss, tid);
+            } else {
+                const LayerPtrs &prev = sm.layers[layer - 1];
+                NormW nw;
+                norm_prefetch(nw, prev.post_ff_ln, lp.in_ln, p.H, tid);
+                if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+                // x = r + norm(mlp, post_ff) (layers.mojo:216-220), xs = norm(x, input_layernorm) (195)
+                stage_norm<NB>(p.r, p.mlp_raw, prev.post_ff_ln, lp.in_ln, nw, out_h, p.H, p.inv_h, g.Kp, sm.xs, ss, tid);
+            }
+            gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+                             GemvOut{p.qkv, p.qkv_rows});
+            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+        } else if (kind == PH_ATT) {
+            if (tid == 0) att_rows<NB>(p, lp.is_global != 0, ss.pos, ss.att);
+            consumer_sync(kConsumerThreads);
+            const AttRet r = att_dispatch(p, sm, ss, lp, layer, ph, ss.att, tile, ok, tid, has_dep);
+            tile = r.tile;
+            ok = r.ok;
+            cta_signal(ctr_phase(p, ph), r.done, ss, tid);
+        } else if (kind == PH_O) {
+            GemvGeom<WT> g;
+            gemv_geom<WT>(p, lp, kind, ph, g);
+            if (tid == 0) att_rows<NB>(p, lp.is_global != 0, ss.pos, ss.att);
+            consumer_sync(kConsumerThreads);
+            const AttRows &a = ss.att;
+            if (has_dep)
+                ok = cta_wait(ctr_phase(p, ph - 1), static_cast<uint32_t>(a.nitems), p.err, 100 + ph, ss, tid) && ok;
+            att_combine(p, a, g.Kp, sm.xs, tid);
+            gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+                             GemvOut{p.o_raw, p.H});
+            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+        } else if (kind == PH_GU) {
+            GemvGeom<WT> g;
+            gemv_geom<WT>(p, lp, kind, ph, g);
+            NormW nw;
+            norm_prefetch(nw, lp.post_attn_ln, lp.pre_ff_ln, p.H, tid);
+            if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+            // r = h + norm(o_raw, post_attn) (layers.mojo:202-207); xs = norm(r, pre_ff) (209-210)
+            stage_norm<NB>(p.h, p.o_raw, lp.post_attn_ln, lp.pre_ff_ln, nw, blockIdx.x == 0 ? p.r : nullptr, p.H,
+                           p.inv_h, g.Kp, sm.xs, ss, tid);
+            gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+                             GemvOut{p.act, p.Ip});
+            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+        } else if (kind == PH_D) {
+            GemvGeom<WT> g;
+            gemv_geom<WT>(p, lp, kind, ph, g);
+            if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+            // down_proj input: act rows, 8 float4 loads in flight per thread
+            for (int b = 0; b < B; ++b) {
+                for (int i0 = 0; i0 < g.Kp; i0 += 8 * 4 * kConsumerThreads) {
+                    float4 v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int i = i0 + (tid + j * kConsumerThreads) * 4;
+                        v[j] = i < g.Kp ? __ldcg(reinterpret_cast<const float4 *>(p.act + static_cast<int64_t>(b) * p.Ip + i))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int i = i0 + (tid + j * kConsumerThreads) * 4;
+                        if (i < g.Kp) *reinterpret_cast<float4 *>(sm.xs + b * g.Kp + i) = v[j];
+                    }
+                }
+            }
+            consumer_sync(kConsumerThreads);
+            gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+                             GemvOut{p.mlp_raw, p.H});
+            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+        } else if (kind == PH_LMH) {
+            GemvGeom<WT> g;
+            gemv_geom<WT>(p, lp, kind, ph, g);
+            if (p.lm_mode != kLmNone) {
+                NormW nw;
+                norm_prefetch(nw, lp.post_ff_ln, p.final_norm, p.H, tid);
+                if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+                // x = r + norm(mlp_raw, post_ff); xs = norm(x, final norm) (layers.mojo:283-285)
+                stage_norm<NB>(p.r, p.mlp_raw, lp.post_ff_ln, p.final_norm, nw, nullptr, p.H, p.inv_h, g.Kp, sm.xs, ss,
+                               tid);
+            }
+            if (p.lm_mode == kLmEmbed) {
+                if (blockIdx.x == 0 && ok)
+                    for (int b = 0; b < B; ++b)
+                        if (ss.active[b])
+                            for (int i = tid; i < p.H; i += kConsumerThreads)
+                                p.emb_acc[static_cast<int64_t>(b) * p.H + i] += sm.xs[b * g.Kp + i];
+            } else if (p.lm_mode == kLmLogits) {
+                gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+                                 GemvOut{p.logits, p.V});
+                if (p.topk > 0) {
+                    consumer_sync(kConsumerThreads);
+                    lm_topk(p, sm, g.row0, g.nrows, tid);
+                }
+            }
+            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+        } else {  // PH_SAMPLE
+            const int b = blockIdx.x;
+            if (b < B) {
+                int32_t token = -1;
+                if (p.sample && p.lm_mode == kLmLogits && p.topk > 0) {
+                    if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+                    token = row_draw(p, sm, b, ok, tid);
+                }
+                if (tid == 0 && ok) {
+                    if (token >= 0) {
+                        p.tok[b] = token;
+                        if (p.out_tokens) p.out_tokens[b] = token;
+                    }
+                    if (ss.active[b]) p.pos[b] = ss.pos[b] + 1;
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- producer
+template <typename WT, int NB>
+__device__ void producer_run(const DecodeParams &p, const Smem &sm, SmallSmem &ss) {
+    const int G = gridDim.x;
+    const uint64_t pol_w = policy_evict_first();
+    uint32_t tile = 0, issued = 0;
+    bool ok = true;
+    const uint32_t S = static_cast<uint32_t>(p.S);
+    const uint32_t inflight = static_cast<uint32_t>(min(max(p.max_inflight, 1), p.S));
+    // Slot for tile t: its stage was released by the consumers (tile t - S), and
+    // at most `inflight` copies are outstanding (tile t - inflight has landed).
+    auto acquire_slot = [&](uint32_t t) -> bool {
+        if (t >= S && !mbar_wait(&sm.empty[t % S], ((t / S) - 1) & 1u, p.err, kErrTimeoutEmpty | 1u)) return false;
+        if (t >= inflight) {
+            const uint32_t u = t - inflight;
+            if (u < issued && !mbar_wait(&sm.full[u % S], (u / S) & 1u, p.err, kErrTimeoutFull | 3u)) return false;
+        }
+        return true;
+    };
+    for (int ph = p.ph_begin; ph < p.ph_end; ++ph) {
+        int kind, layer;
+        phase_of(ph, p.L, kind, layer);
+        const LayerPtrs &lp = sm.layers[layer];
+        trace_mark(trace_slot(p, ph, kTrProdStart));
+        if (kind == PH_ATT) {
+            AttRows &a = ss.att_p;
+            att_rows<NB>(p, lp.is_global != 0, ss.pos, a);
+            const int slot = cta_slot(ph);
+            for (int item = slot; item < a.nitems; item += G) {
+                int b, kvh, c;
+                att_item(p, a, item, b, kvh, c);
+                const int pos = ss.pos[b];
+                const int t_begin = a.lo[b] + c * p.att_ch;
+                const int t_end = min(t_begin + p.att_ch, pos + 1);
+                const size_t kvbase = static_cast<size_t>(layer) * p.kv_layer_stride +
+                                      static_cast<size_t>(b) * p.kv_row_stride +
+                                      static_cast<size_t>(kvh) * p.kv_head_stride;
+                for (int ts = t_begin; ts < t_end; ts += kAttTile, ++tile) {
+                    const int st = static_cast<int>(tile % S);
+                    ok = ok && acquire_slot(tile);
+                    const int te = min(ts + kAttTile, t_end);
+                    const int ncached = max(0, min(te, pos) - ts);  // row `pos` is computed, not read
+                    const uint32_t bytes = static_cast<uint32_t>(ncached * p.hdp * 4);
+                    if (!ok) continue;
+                    issued = tile + 1;
+                    mbar_arrive_expect_tx(&sm.full[st], 2u * bytes);
+                    if (bytes) {
+                        unsigned char *dst = sm.ring + static_cast<size_t>(st) * kStageBytes;
+                        const size_t off = kvbase + static_cast<size_t>(ts) * p.hdp;
+                        bulk_g2s(dst, p.kc + off, bytes, &sm.full[st], pol_w);
+                        bulk_g2s(dst + static_cast<size_t>(kAttTile) * p.hdp * 4, p.vc + off, bytes, &sm.full[st],
+                                 pol_w);
+                    }
+                }
+            }
+        } else if (kind != PH_SAMPLE) {
+            GemvGeom<WT> g;
+            gemv_geom<WT>(p, lp, kind, ph, g);
+            // this CTA's tiles are contiguous in the tiled layout: one bulk copy per tile
+            const uint32_t bytes = static_cast<uint32_t>(g.tile_elems * sizeof(WT));
+            const int ntiles = g.ngroups * g.nseg;
+            if (p.pf_tiles > 0 && ok && ntiles > static_cast<int>(S)) {
+                // L2 prefetch of the part of this phase the ring cannot hold yet
+                const char *from = reinterpret_cast<const char *>(g.tiles) + static_cast<size_t>(S) * bytes;
+                size_t left = static_cast<size_t>(ntiles - static_cast<int>(S)) * bytes;
+                for (; left > 0;) {
+                    const uint32_t nb = static_cast<uint32_t>(min(left, static_cast<size_t>(1u << 20)));
+                    bulk_prefetch_l2(from, nb);
+                    from += nb;
+                    left -= nb;
+                }
+            }
+            for (int t = 0; t < ntiles; ++t, ++tile) {
+                const int st = static_cast<int>(tile % S);
+                ok = ok && acquire_slot(tile);
+                if (!ok) continue;
+                issued = tile + 1;
+                mbar_arrive_expect_tx(&sm.full[st], bytes);
+                bulk_g2s(sm.ring + static_cast<size_t>(st) * kStageBytes, g.tiles + static_cast<int64_t>(t) * g.tile_elems,
+                         bytes, &sm.full[st], pol_w);
+            }
+        }
+        trace_mark(trace_slot(p, ph, kTrProdEnd));
+    }
+    // Drain: copies still in flight must land before the CTA exits.
+    const uint32_t first = issued > S ? issued - S : 0u;
+    for (uint32_t t = first; t < issued; ++t) {
+        if (!mbar_wait_drain(&sm.full[t % S], (t / S) & 1u)) set_error(p.err, kErrTimeoutDrain);
+    }
+}
+
+// ---------------------------------------------------------------- the kernel
+template <typename WT, int NB>
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ SmallSmem ss;
+    // The pointer block lives in shared memory: helpers take it by reference,
+    // and a local copy would turn each of their reads into a local-memory load.
+    __shared__ Smem sm;
+    Smem sl;
+    {
+        uintptr_t base = reinterpret_cast<uintptr_t>(smem_raw);
+        base = (base + 127) & ~static_cast<uintptr_t>(127);
+        sl.ring = reinterpret_cast<unsigned char *>(base);
+        sl.xs = reinterpret_cast<float *>(sl.ring + static_cast<size_t>(p.S) * kStageBytes);
+        sl.full = reinterpret_cast<uint64_t *>(sl.xs + p.xs_floats);
+        sl.empty = sl.full + p.S;
+        sl.layers = reinterpret_cast<LayerPtrs *>(sl.empty + p.S);
+    }
+    if (threadIdx.x == 0) sm = sl;
+    const int tid = threadIdx.x;
+    const int G = gridDim.x;
+
+    if (tid == 0) {
+        for (int s = 0; s < p.S; ++s) {
+            mbar_init(&sl.full[s], 1);
+            mbar_init(&sl.empty[s], kConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(p.layers);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(sl.layers);
+        const int nw = p.L * static_cast<int>(sizeof(LayerPtrs) / 4);
+        for (int i = tid; i < nw; i += kThreads) dst[i] = src[i];
+    }
+    if (tid < p.B) {
+        const int b = tid;
+        int active = 1;
+        int tok;
+        if (p.ids != nullptr) {
+            const int nv = p.nvalid[b];
+            active = p.step_t < nv;
+            const int ti = min(p.step_t, max(nv - 1, 0));
+            tok = p.ids[static_cast<int64_t>(b) * p.ids_ld + ti];
+        } else {
+            tok = p.tok[b];
+        }
+        if (tok < 0 || tok >= p.V) {
+            set_error(p.err, kErrBadToken | static_cast<uint32_t>(b));
+            tok = 0;
+        }
+        int pos = p.pos[b];
+        if (pos < 0 || pos >= p.cap) {
+            if (active) set_error(p.err, kErrBadPos | static_cast<uint32_t>(b));
+            active = 0;
+            pos = min(max(pos, 0), p.cap - 1);
+        }
+        ss.pos[b] = pos;
+        ss.tok[b] = tok;
+        ss.active[b] = active;
+    }
+    __syncthreads();
+    uint64_t *tr_kernel =
+        p.trace ? p.trace + static_cast<size_t>(G) * p.n_phases * kTraceSlots + 2 * blockIdx.x : nullptr;
+    if (tid == 0) {
+        trace_mark(tr_kernel);
+        // SM clock cross-check for the timeline: cycles at kernel begin in the SAMPLE phase's spare slot
+        uint64_t *ck = trace_slot(p, p.n_phases - 1, 6);
+        if (ck) *ck = clock64();
+    }
+
+    if ((tid >> 5) == kConsumerWarps) {
+        if ((tid & 31) == 0) producer_run<WT, NB>(p, sm, ss);
+    } else {
+        consumer_run<WT, NB>(p, sm, ss, tid);
+    }
+
+    // ---- exit: the last CTA out resets the counters used by this launch.
+    __syncthreads();
+    if (tid == 0) {
+        trace_mark(tr_kernel ? tr_kernel + 1 : nullptr);
+        uint64_t *ck = trace_slot(p, p.n_phases - 1, 7);
+        if (ck) *ck = clock64();
+        __threadfence();
+        const uint32_t old = atomicAdd(ctr_exit(p), 1u);
+        if (old == static_cast<uint32_t>(G - 1)) {
+            __threadfence();
+            for (int ph = p.ph_begin; ph < p.ph_end; ++ph) *ctr_phase(p, ph) = 0u;
+            *ctr_exit(p) = 0u;
+            __threadfence();
+        }
+    }
+}
+
+// ---------------------------------------------------------------- host launch (per row count)
+// Static shared memory of the kernel (SmallSmem and the pointer block) in bytes.
+template <typename WT, int NB>
+size_t decode_static_smem_nb() {
+    cudaFuncAttributes a;
+    if (cudaFuncGetAttributes(&a, decode_kernel<WT, NB>) != cudaSuccess) return 1024;
+    return a.sharedSizeBytes;
+}
+
+template <typename WT, int NB>
+cudaError_t decode_prepare_nb(size_t dynamic_smem) {
+    return cudaFuncSetAttribute(decode_kernel<WT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(dynamic_smem));
+}
+
+template <typename WT, int NB>
+int decode_occupancy_nb(size_t smem) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<WT, NB>, kThreads, smem) != cudaSuccess)
+        return 0;
+    return n;
+}
+
+template <typename WT, int NB>
+cudaError_t decode_launch_nb(const DecodeParams &p, int grid, size_t smem, cudaStream_t stream, bool cooperative) {
+    if (cooperative) {
+        void *args[] = {const_cast<DecodeParams *>(&p)};
+        return cudaLaunchCooperativeKernel(reinterpret_cast<void *>(decode_kernel<WT, NB>), dim3(grid),
+                                           dim3(kThreads), args, smem, stream);
+    }
+    decode_kernel<WT, NB><<<grid, kThreads, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace mg
+
+// Explicit instantiation of the host helpers (and so of the kernel) for one row count.
+#define MG_DECODE_INSTANTIATE_WT(WT, NB)                                                                       \
+    namespace mg {                                                                                             \
+    template size_t decode_static_smem_nb<WT, NB>();                                                           \
+    template cudaError_t decode_prepare_nb<WT, NB>(size_t);                                                    \
+    template int decode_occupancy_nb<WT, NB>(size_t);                                                          \
+    template cudaError_t decode_launch_nb<WT, NB>(const DecodeParams &, int, size_t, cudaStream_t, bool);      \
+    }
+#define MG_DECODE_INSTANTIATE(NB)             \
+    MG_DECODE_INSTANTIATE_WT(float, NB)       \
+    MG_DECODE_INSTANTIATE_WT(__nv_bfloat16, NB)

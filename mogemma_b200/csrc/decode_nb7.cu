@@ -1,0 +1,4 @@
+// decode_nb7.cu -- the decode kernel (decode_kernel.cuh) for 7 batch row(s), fp32 and bf16 weights.
+#include "decode_kernel.cuh"
+
+MG_DECODE_INSTANTIATE(7)
