@@ -22,6 +22,7 @@ constexpr int kMaxHeadDim = 256;
 constexpr int kMaxQPerKv = 8;
 constexpr int kMaxTopK = 64;         // fused top-k width
 constexpr int kAttTile = 16;         // positions per attention tile
+constexpr int kPartHead = 4;         // floats before a split-KV partial's acc: m, l, 2 pad (16-byte aligned acc)
 constexpr int kMaxChunks = 32;       // split-KV chunks per (row, kv head); one warp lane each in the combine
 
 enum PhaseKind : int { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_D = 4, PH_LMH = 5, PH_SAMPLE = 6 };

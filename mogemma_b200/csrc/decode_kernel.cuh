@@ -154,7 +154,7 @@ __device__ __forceinline__ void att_item(const DecodeParams &p, const AttRows &a
 
 __device__ __forceinline__ float *att_part(const DecodeParams &p, int b, int kvh, int c) {
     const int Gq = p.Hq / p.Hkv;
-    return p.attn_part + ((static_cast<int64_t>(b) * p.Hkv + kvh) * kMaxChunks + c) * Gq * (p.hd + 2);
+    return p.attn_part + ((static_cast<int64_t>(b) * p.Hkv + kvh) * kMaxChunks + c) * Gq * (p.hd + kPartHead);
 }
 
 // ---------------------------------------------------------------- shared memory
@@ -682,7 +682,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
         if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttTiles));
         // ---- partial (m, l, acc) of this chunk; combined in the o_proj prologue
         float *part = att_part(p, b, kvh, c);
-        const int part_ld = hd + 2;
+        const int part_ld = hd + kPartHead;
         if (ntq > 1) {  // fold the position classes
             float *red = rope_s + B * hd;  // [ntq][Gq][hd]
             if (pv_on)
@@ -704,7 +704,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
         if (pv_q == 0) {
 #pragma unroll
             for (int h = 0; h < kQ; ++h)
-                if (h < Gq) part[h * part_ld + 2 + pv_d] = acc[h];
+                if (h < Gq) part[h * part_ld + kPartHead + pv_d] = acc[h];
         }
         if (tid < Gq) {
             part[tid * part_ld + 0] = m_s[tid];
@@ -736,51 +736,97 @@ __device__ __forceinline__ AttRet att_dispatch(const DecodeParams &p, const Smem
 
 // o_proj input from the split-KV partials of every (row, kv head):
 //   w_c = exp(m_c - M) / sum_c l_c exp(m_c - M);  x[b][h*hd+d] = sum_c w_c * acc_c[d]
-// One warp per (row, q head): lanes hold one chunk's weight, then run over
-// head dims with eight chunks of loads in flight.
+// One warp per (row, q head, half of the head dims): lane c holds chunk c's
+// m and l, and every chunk's 4-dim slice of acc is loaded as a float4 in the
+// same round trip (16 chunks per batch).  Head dims that are not a multiple
+// of 4 take the scalar path.
 static __device__ __noinline__ void att_combine(const DecodeParams &p, const AttRows &a, int Kp, float *xs, int tid) {
     const int lane = tid & 31, warp = tid >> 5;
     const int Gq = p.Hq / p.Hkv, hd = p.hd, B = p.B;
-    const int part_ld = hd + 2;
+    const int part_ld = hd + kPartHead;
     const int64_t cstride = static_cast<int64_t>(Gq) * part_ld;
-    constexpr int kDims = kMaxHeadDim / 32;
-    constexpr int kCh = 8;
-    for (int bh = warp; bh < B * p.Hq; bh += kConsumerWarps) {
-        const int b = bh / p.Hq, hq = bh - b * p.Hq;
-        const int kvh = hq / Gq, hl = hq - kvh * Gq;
-        const int nch = a.nch[b];
-        const float *base = att_part(p, b, kvh, 0) + hl * part_ld;
-        float m = -INFINITY, l = 0.f;
-        if (lane < nch) {
-            m = __ldcg(base + lane * cstride);
-            l = __ldcg(base + lane * cstride + 1);
-        }
-        const float M = warp_max(m);
-        const float e = lane < nch ? expf(m - M) : 0.f;
-        const float w = e / warp_sum(l * e);
-        float x[kDims];
+    if (hd % 4 == 0) {
+        constexpr int kBatch = 16;
+        const int halves = hd > 128 ? 2 : 1;
+        const int dpt = hd / halves;  // dims per task, <= 128: one float4 per lane
+        for (int task = warp; task < B * p.Hq * halves; task += kConsumerWarps) {
+            const int bh = task / halves, hf = task - bh * halves;
+            const int b = bh / p.Hq, hq = bh - b * p.Hq;
+            const int kvh = hq / Gq, hl = hq - kvh * Gq;
+            const int nch = a.nch[b];
+            const float *base = att_part(p, b, kvh, 0) + hl * part_ld;
+            const int d0 = hf * dpt + lane * 4;
+            const bool on = lane * 4 < dpt;
+            float m = -INFINITY, l = 0.f;
+            if (lane < nch) {
+                m = __ldcg(base + lane * cstride);
+                l = __ldcg(base + lane * cstride + 1);
+            }
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            float w = 0.f;
+            for (int c0 = 0; c0 < nch; c0 += kBatch) {
+                float4 v[kBatch];
 #pragma unroll
-        for (int i = 0; i < kDims; ++i) x[i] = 0.f;
-        for (int c0 = 0; c0 < nch; c0 += kCh) {
-            float v[kCh][kDims];
-#pragma unroll
-            for (int u = 0; u < kCh; ++u)
-#pragma unroll
-                for (int i = 0; i < kDims; ++i) {
-                    const int d = lane + 32 * i;
-                    v[u][i] = (c0 + u < nch && d < hd) ? __ldcg(base + (c0 + u) * cstride + 2 + d) : 0.f;
+                for (int u = 0; u < kBatch; ++u)
+                    v[u] = (on && c0 + u < nch)
+                               ? __ldcg(reinterpret_cast<const float4 *>(base + (c0 + u) * cstride + kPartHead + d0))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (c0 == 0) {
+                    const float M = warp_max(m);
+                    const float e = lane < nch ? expf(m - M) : 0.f;
+                    w = __fdividef(e, warp_sum(l * e));
                 }
 #pragma unroll
-            for (int u = 0; u < kCh; ++u) {
-                const float wu = __shfl_sync(0xffffffffu, w, (c0 + u) & 31);
-#pragma unroll
-                for (int i = 0; i < kDims; ++i) x[i] += wu * v[u][i];
+                for (int u = 0; u < kBatch; ++u) {
+                    const float wu = __shfl_sync(0xffffffffu, w, (c0 + u) & 31);
+                    x.x += wu * v[u].x;
+                    x.y += wu * v[u].y;
+                    x.z += wu * v[u].z;
+                    x.w += wu * v[u].w;
+                }
             }
+            if (on) *reinterpret_cast<float4 *>(xs + b * Kp + hq * hd + d0) = x;
         }
+    } else {
+        constexpr int kDims = kMaxHeadDim / 32;
+        constexpr int kCh = 8;
+        for (int bh = warp; bh < B * p.Hq; bh += kConsumerWarps) {
+            const int b = bh / p.Hq, hq = bh - b * p.Hq;
+            const int kvh = hq / Gq, hl = hq - kvh * Gq;
+            const int nch = a.nch[b];
+            const float *base = att_part(p, b, kvh, 0) + hl * part_ld;
+            float m = -INFINITY, l = 0.f;
+            if (lane < nch) {
+                m = __ldcg(base + lane * cstride);
+                l = __ldcg(base + lane * cstride + 1);
+            }
+            const float M = warp_max(m);
+            const float e = lane < nch ? expf(m - M) : 0.f;
+            const float w = __fdividef(e, warp_sum(l * e));
+            float x[kDims];
 #pragma unroll
-        for (int i = 0; i < kDims; ++i) {
-            const int d = lane + 32 * i;
-            if (d < hd) xs[b * Kp + hq * hd + d] = x[i];
+            for (int i = 0; i < kDims; ++i) x[i] = 0.f;
+            for (int c0 = 0; c0 < nch; c0 += kCh) {
+                float v[kCh][kDims];
+#pragma unroll
+                for (int u = 0; u < kCh; ++u)
+#pragma unroll
+                    for (int i = 0; i < kDims; ++i) {
+                        const int d = lane + 32 * i;
+                        v[u][i] = (c0 + u < nch && d < hd) ? __ldcg(base + (c0 + u) * cstride + kPartHead + d) : 0.f;
+                    }
+#pragma unroll
+                for (int u = 0; u < kCh; ++u) {
+                    const float wu = __shfl_sync(0xffffffffu, w, (c0 + u) & 31);
+#pragma unroll
+                    for (int i = 0; i < kDims; ++i) x[i] += wu * v[u][i];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kDims; ++i) {
+                const int d = lane + 32 * i;
+                if (d < hd) xs[b * Kp + hq * hd + d] = x[i];
+            }
         }
     }
     for (int o = tid; o < B * Kp; o += kConsumerThreads) {

@@ -467,7 +467,7 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     TRY(dalloc(m, &m->o_raw, static_cast<size_t>(B) * m->H));
     TRY(dalloc(m, &m->act, static_cast<size_t>(B) * m->Ip));
     TRY(dalloc(m, &m->mlp_raw, static_cast<size_t>(B) * m->H));
-    TRY(dalloc(m, &m->attn_part, static_cast<size_t>(B) * m->Hkv * m->max_ch * Gq * (hd + 2)));
+    TRY(dalloc(m, &m->attn_part, static_cast<size_t>(B) * m->Hkv * m->max_ch * Gq * (hd + kPartHead)));
     TRY(dalloc(m, &m->attn_out, static_cast<size_t>(B) * m->Ap));
     TRY(dalloc(m, &m->logits, static_cast<size_t>(B) * m->V));
     TRY(dalloc(m, &m->emb_acc, static_cast<size_t>(B) * m->H));
