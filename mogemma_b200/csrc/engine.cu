@@ -589,10 +589,10 @@ static DecodeParams base_params(mg_model *m, int B) {
     return p;
 }
 
-// Positions per split-KV chunk: about 16 chunks per (row, kv head), never more
+// Positions per split-KV chunk: up to kMaxChunks chunks per (row, kv head) spread over the CTAs, never more
 // than kMaxChunks for the longest row of the launch, whole tiles.
 static int att_chunk(const mg_model *m, int B, int max_ctx) {
-    const int target = std::max(1, std::min(16, m->G / std::max(1, B * m->Hkv)));
+    const int target = std::max(1, std::min(kMaxChunks, m->G / std::max(1, B * m->Hkv)));
     int ch = std::max((max_ctx + target - 1) / target, (max_ctx + kMaxChunks - 1) / kMaxChunks);
     ch = (ch + kAttTile - 1) / kAttTile * kAttTile;
     return std::max(ch, kAttTile);
