@@ -83,9 +83,9 @@ typedef struct mg_options {
     void *stream;             /* cudaStream_t to run on; NULL: the library creates one */
     int32_t decode_path;      /* 0: persistent decode kernel; 1: one launch per phase */
     int32_t tp_rank;          /* tensor-parallel rank (0 when tp_size == 1) */
-    int32_t tp_size;          /* tensor-parallel degree */
+    int32_t tp_size;          /* tensor-parallel degree (1..8); one process per GPU, see mg_tp_connect */
     int32_t reserved0;
-    const void *nccl_id;      /* 128-byte ncclUniqueId when tp_size > 1 */
+    const void *reserved1;
 } mg_options;
 
 typedef struct mg_model_info {
@@ -187,7 +187,24 @@ mg_status mg_read_kv(const mg_model *m, int32_t layer, int32_t row, int32_t pos,
  * the stamps of the most recent launch; *n_out receives the element count. */
 mg_status mg_trace_enable(mg_model *m, int32_t on);
 mg_status mg_trace_read(mg_model *m, uint64_t *out_host, int64_t capacity, int64_t *n_out);
-mg_status mg_nccl_unique_id(void *out128);
+
+/* ---- tensor parallelism (no counterpart in the reference, which runs one
+ * CPU thread; the sharding follows the Gemma layout: q heads and the kv heads
+ * they use, o_proj and down_proj split along their inputs, gate/up along their
+ * outputs, lm_head along the vocabulary) ----
+ * A model created with tp_size = T > 1 holds rank tp_rank's shard.  Its decode
+ * kernel exchanges the o_proj / down_proj partial sums and the lm_head top-k
+ * candidates through the other ranks' exchange buffers (peer memory over
+ * NVLink) inside the same launch.  Before the first step every rank exports its
+ * buffer's IPC handle, the caller gathers the T handles in rank order (for
+ * example with torch.distributed over NCCL) and passes them to mg_tp_connect.
+ * All ranks must then issue the same sequence of steps. */
+#define MG_TP_HANDLE_BYTES 64
+mg_status mg_tp_ipc_handle(const mg_model *m, void *out /* MG_TP_HANDLE_BYTES */);
+mg_status mg_tp_connect(mg_model *m, const void *handles /* n * MG_TP_HANDLE_BYTES, rank order */, int32_t n);
+/* Unmaps the other ranks' buffers.  Every rank calls it (after its last step)
+ * before any rank destroys its model, so no buffer is freed while mapped. */
+mg_status mg_tp_disconnect(mg_model *m);
 
 #ifdef __cplusplus
 }

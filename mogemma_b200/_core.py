@@ -77,7 +77,7 @@ class Options(ctypes.Structure):
         ("tp_rank", ctypes.c_int32),
         ("tp_size", ctypes.c_int32),
         ("reserved0", ctypes.c_int32),
-        ("nccl_id", ctypes.c_void_p),
+        ("reserved1", ctypes.c_void_p),
     ]
 
 
@@ -126,12 +126,15 @@ _lib.mg_sample.argtypes = [_F32P, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER
                            ctypes.c_uint64, _I32P]
 _lib.mg_embed.argtypes = [_P, _I32P, _I32P, ctypes.c_int32, ctypes.c_int32, _F32P]
 _lib.mg_read_kv.argtypes = [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _F32P, _F32P]
-_lib.mg_nccl_unique_id.argtypes = [_P]
+_lib.mg_tp_ipc_handle.argtypes = [_P, _P]
+_lib.mg_tp_connect.argtypes = [_P, _P, ctypes.c_int32]
+_lib.mg_tp_disconnect.argtypes = [_P]
+TP_HANDLE_BYTES = 64  # MG_TP_HANDLE_BYTES
 _lib.mg_trace_enable.argtypes = [_P, ctypes.c_int32]
 _lib.mg_trace_read.argtypes = [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)]
 for _f in ("mg_model_create", "mg_model_info_get", "mg_model_destroy", "mg_set_pos", "mg_get_pos", "mg_step",
            "mg_prefill", "mg_generate", "mg_set_tokens", "mg_sample", "mg_embed", "mg_read_kv",
-           "mg_nccl_unique_id", "mg_trace_enable", "mg_trace_read"):
+           "mg_tp_ipc_handle", "mg_tp_connect", "mg_tp_disconnect", "mg_trace_enable", "mg_trace_read"):
     getattr(_lib, _f).restype = ctypes.c_int
 
 
@@ -208,6 +211,21 @@ class ModelHandle:
         slots = (buf.size - 2 * g) // (g * nph)
         return buf[: g * nph * slots].reshape(g, nph, slots), buf[g * nph * slots:].reshape(g, 2)
 
+    def tp_handle(self) -> bytes:
+        """IPC handle of this rank's exchange buffer (tensor-parallel models)."""
+        buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
+        _check(_lib.mg_tp_ipc_handle(self.ptr, ctypes.cast(buf, _P)))
+        return buf.raw
+
+    def tp_connect(self, handles: Sequence[bytes]) -> None:
+        """Map the other ranks' exchange buffers (handles in rank order)."""
+        blob = b"".join(handles)
+        if len(blob) != TP_HANDLE_BYTES * len(handles):
+            msg = "every handle must be TP_HANDLE_BYTES long"
+            raise ValueError(msg)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        _check(_lib.mg_tp_connect(self.ptr, ctypes.cast(buf, _P), len(handles)))
+
     def get_pos(self) -> list[int]:
         out = np.zeros(8, np.int32)
         _check(_lib.mg_get_pos(self.ptr, out.ctypes.data_as(_I32P), 8))
@@ -259,8 +277,8 @@ def create_model(metadata: dict[str, Any], **options: Any) -> ModelHandle:
     o.seed = int(options.get("seed", _env_int("MOGEMMA_B200_SEED", 0))) & 0xFFFFFFFFFFFFFFFF
     o.stream = options.get("stream")
     o.decode_path = int(options.get("decode_path", _env_int("MOGEMMA_B200_DECODE_PATH", 0)))
-    o.tp_rank = 0
-    o.tp_size = 1
+    o.tp_rank = int(options.get("tp_rank", 0))
+    o.tp_size = int(options.get("tp_size", 1))
     out = _P()
     _check(_lib.mg_model_create(descs, len(names), ctypes.byref(o), ctypes.byref(out)))
     info = ModelInfo()
@@ -302,6 +320,44 @@ def init_model(metadata: dict[str, Any], **options: Any) -> dict[str, Any]:
         "pos": 0,
         "_handle": handle,
     }
+
+
+def gather_handles(handle: bytes, group: Any = None) -> list[bytes]:
+    """All ranks' exchange-buffer handles in rank order, over torch.distributed."""
+    import torch.distributed as dist  # noqa: PLC0415
+
+    out: list[Any] = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, handle, group=group)
+    return [bytes(h) for h in out]
+
+
+def init_model_tp(metadata: dict[str, Any], group: Any = None, **options: Any) -> dict[str, Any]:
+    """``init_model`` for one rank of a tensor-parallel group (one process per
+    GPU, torch.distributed initialised).  Every rank loads the same checkpoint
+    and keeps its shard; the exchange buffers are connected before returning."""
+    import torch.distributed as dist  # noqa: PLC0415
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    llm = init_model(metadata, tp_rank=rank, tp_size=world, **options)
+    if world > 1:
+        h = llm["_handle"]
+        h.tp_connect(gather_handles(h.tp_handle(), group))
+        dist.barrier(group)
+    return llm
+
+
+def close_tp(llm: dict[str, Any], group: Any = None) -> None:
+    """Destroy one rank's tensor-parallel model: every rank unmaps its peers'
+    buffers before any rank frees its own."""
+    import torch.distributed as dist  # noqa: PLC0415
+
+    h = llm["_handle"]
+    if int(h.info.tp_size) > 1:
+        dist.barrier(group)
+        _check(_lib.mg_tp_disconnect(h.ptr))
+        dist.barrier(group)
+    h.close()
 
 
 def _handle(llm: dict[str, Any]) -> ModelHandle:

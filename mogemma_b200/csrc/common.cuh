@@ -49,6 +49,16 @@ __device__ __forceinline__ void red_release_add_u32(uint32_t *p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// System-scope variants for counters that other GPUs increment over NVLink.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_release_sys_add_u64(uint64_t *p, uint64_t v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void set_error(uint32_t *err, uint32_t code) { atomicCAS(err, 0u, code); }
 
 // Wait until *ctr >= target (acquire).  Returns false on error/timeout.
@@ -60,6 +70,24 @@ __device__ __forceinline__ bool wait_counter_geq(const uint32_t *ctr, uint32_t t
         if (ld_acquire_u32(ctr) >= target) return true;
         // the error word and the clock are checked every 8th poll: each check
         // is another dependent round trip between two polls
+        if ((n & 7u) == 0u) {
+            if (ld_relaxed_u32(err) != 0u) return false;
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+                set_error(err, kErrTimeoutCounter | site);
+                return false;
+            }
+        }
+    }
+}
+
+// Wait until the 64-bit counter *ctr (incremented by this and peer GPUs)
+// reaches target (acquire at system scope).  Returns false on error/timeout.
+__device__ __forceinline__ bool wait_counter_geq_sys(const uint64_t *ctr, uint64_t target, uint32_t *err,
+                                                     uint32_t site) {
+    if (ld_acquire_sys_u64(ctr) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; ++n) {
+        if (ld_acquire_sys_u64(ctr) >= target) return true;
         if ((n & 7u) == 0u) {
             if (ld_relaxed_u32(err) != 0u) return false;
             if (globaltimer_ns() - t0 > kWaitBudgetNs) {

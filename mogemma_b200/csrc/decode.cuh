@@ -18,6 +18,7 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kStageBytes = 36864;   // one ring stage
 constexpr int kMaxRows = 8;          // batch rows per persistent launch
+constexpr int kMaxTp = 8;            // tensor-parallel ranks
 constexpr int kMaxHeadDim = 256;
 constexpr int kMaxQPerKv = 8;
 constexpr int kMaxTopK = 64;         // fused top-k width
@@ -100,6 +101,21 @@ struct DecodeParams {
     uint64_t *trace;
     float att_scale;    // 1 / sqrt(head_dim), as the reference computes it (layers.mojo:65)
     float emb_scale;    // sqrt(H) (layers.mojo:247-251)
+
+    // tensor parallelism (tp > 1): this rank holds q heads, kv heads, FFN rows
+    // and vocabulary rows of its shard (the dimensions above are the shard's).
+    // The row-split o_proj and down_proj write their partial [B][H] rows into
+    // every rank's exchange buffer (peer memory over NVLink) and count on each
+    // rank's exchange counters; lm_head candidates are exchanged the same way.
+    int32_t tp, tp_rank;
+    int32_t V_full;          // vocabulary of the whole model (token id range)
+    int32_t vocab_off;       // first vocabulary row of this rank's lm_head shard
+    int32_t xB;              // rows per source block in the exchange buffers (the model's max batch)
+    int32_t pad3_;
+    uint64_t xep;            // exchanges of earlier forwards: layer l exchanges index xep + l
+    uint64_t lm_ep;          // candidate exchanges of earlier forwards
+    char *xpeer[kMaxTp];     // exchange buffer of every rank (this rank's own at tp_rank)
+    int64_t x_cnt, x_o, x_d, x_cand;  // byte offsets in an exchange buffer
 };
 
 // trace slots per (CTA, phase)

@@ -167,6 +167,8 @@ struct Smem {
 };
 
 struct SmallSmem {
+    float *xdst_o[kMaxTp];  // tensor parallelism: this rank's receive block on every rank (o_proj)
+    float *xdst_d[kMaxTp];  // (down_proj)
     AttRows att;    // consumers' split of the current attention phase
     AttRows att_p;  // the producer's (it runs phases ahead)
     int pos[kMaxRows];
@@ -231,10 +233,13 @@ __device__ __forceinline__ void norm_prefetch(NormW &nw, const float *w_add, con
 // (when out != null);  xs[b] <- rmsnorm(x) * (1 + w_next), zero padded to Kp.
 // base/add rows ([NB][H] in global memory) were written by other CTAs and are
 // read through L2; all loads of a chunk are issued before any is used.
-template <int NB>
+// XSUM: `add` is nadd per-rank partial blocks (add_stride floats apart) that
+// are summed in rank order, so every rank gets the same bits.
+template <int NB, bool XSUM = false>
 __device__ __forceinline__ void stage_norm(const float *base, const float *add, const float *w_add,
                                            const float *w_next, const NormW &nw, float *out, int H, float inv_h,
-                                           int Kp, float *xs, SmallSmem &ss, int tid) {
+                                           int Kp, float *xs, SmallSmem &ss, int tid, int nadd = 1,
+                                           int64_t add_stride = 0) {
     float sq[NB], sq2[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) sq[b] = sq2[b] = 0.f;
@@ -248,6 +253,23 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
                 const int i = tid + (j0 + j) * kConsumerThreads;
                 v[j] = i < H ? __ldcg(add + static_cast<int64_t>(b) * H + i) : 0.f;
                 bv[j] = i < H ? __ldcg(base + static_cast<int64_t>(b) * H + i) : 0.f;
+            }
+            if constexpr (XSUM) {
+                float t[kMaxTp - 1][kNormPer];
+#pragma unroll
+                for (int r = 1; r < kMaxTp; ++r)
+#pragma unroll
+                    for (int j = 0; j < kNormPer; ++j) {
+                        const int i = tid + (j0 + j) * kConsumerThreads;
+                        t[r - 1][j] = (r < nadd && i < H)
+                                          ? __ldcg(add + r * add_stride + static_cast<int64_t>(b) * H + i)
+                                          : 0.f;
+                    }
+#pragma unroll
+                for (int r = 1; r < kMaxTp; ++r)
+#pragma unroll
+                    for (int j = 0; j < kNormPer; ++j)
+                        if (r < nadd) v[j] += t[r - 1][j];
             }
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
@@ -367,13 +389,56 @@ __device__ __forceinline__ bool cta_wait(const uint32_t *ctr, uint32_t target, u
     return ok;
 }
 
+// ---- tensor parallelism: exchange buffers and counters (see DecodeParams)
+// which: 0 o_proj partials, 1 down_proj partials, 2 lm_head candidates
+__device__ __forceinline__ uint64_t *xcnt(const DecodeParams &p, int rank, int which) {
+    return reinterpret_cast<uint64_t *>(p.xpeer[rank] + p.x_cnt) + which;
+}
+__device__ __forceinline__ float *xrecv(const DecodeParams &p, int rank, int which) {
+    return reinterpret_cast<float *>(p.xpeer[rank] + (which == 0 ? p.x_o : p.x_d));
+}
+// After a phase whose results went to every rank: count this CTA on every
+// rank's counter (system scope; the stores before it are peer stores).
+__device__ __forceinline__ void xsignal(const DecodeParams &p, int which, int tid) {
+    if (tid == 0) {
+        fence_acq_rel_sys();
+        for (int r = 0; r < p.tp; ++r) red_release_sys_add_u64(xcnt(p, r, which), 1ull);
+    }
+}
+// Wait until every CTA of every rank has counted exchange `index` of kind
+// `which` (counters only grow: exchange index e completes at (e + 1) * tp * G).
+__device__ __forceinline__ bool xwait(const DecodeParams &p, int which, uint64_t index, uint32_t site,
+                                      SmallSmem &ss, int tid) {
+    if (tid == 0) {
+        const uint64_t target = (index + 1) * static_cast<uint64_t>(p.tp) * gridDim.x;
+        ss.flag = wait_counter_geq_sys(xcnt(p, p.tp_rank, which), target, p.err, site) ? 1u : 0u;
+        trace_mark(ss.tr_ready);
+    }
+    consumer_sync(kConsumerThreads);
+    const bool ok = ss.flag != 0u;
+    consumer_sync(kConsumerThreads);
+    return ok;
+}
+
 // ---------------------------------------------------------------- GEMV consumer
 // Where a GEMV phase's row results go: out[b * ld + row] = dot, or with a
 // gate/up pair out[b * ld + row] = gelu_erf(gate) * up (ops.mojo:19-22).
+// With tensor parallelism the partial rows of o_proj / down_proj go to every
+// rank's exchange buffer instead: xdst[k] is rank k's receive block of this
+// rank (nx destinations, nx = 0: local out).
 struct GemvOut {
     float *out;
     int64_t ld;
+    float *const *xdst = nullptr;
+    int nx = 0;
 };
+__device__ __forceinline__ void gemv_store(const GemvOut &o, int64_t idx, float v) {
+    if (o.nx) {
+        for (int k = 0; k < o.nx; ++k) o.xdst[k][idx] = v;
+    } else {
+        o.out[idx] = v;
+    }
+}
 
 // NB (rows of x) and PAIR (gate/up) are compile-time so the inner loop is a
 // straight run of 128-bit shared loads and FMAs with accumulators in
@@ -436,10 +501,10 @@ __device__ __forceinline__ void gemv_tiles(const GemvGeom<WT> &g, const float *_
                     const float u = warp_sum(acc2[k][b]);
                     if (lane == 0 && j < nr && ok) {
                         const float gelu = 0.5f * d * (1.0f + erff(d * kInvSqrt2));
-                        o.out[b * o.ld + g.row0 + grp * g.rps + j] = gelu * u;
+                        gemv_store(o, b * o.ld + g.row0 + grp * g.rps + j, gelu * u);
                     }
                 } else {
-                    if (lane == 0 && j < nr && ok) o.out[b * o.ld + g.row0 + grp * g.rps + j] = d;
+                    if (lane == 0 && j < nr && ok) gemv_store(o, b * o.ld + g.row0 + grp * g.rps + j, d);
                 }
             }
         }
@@ -860,12 +925,20 @@ static __device__ __noinline__ void lm_topk(const DecodeParams &p, const Smem &s
             }
         }
         consumer_sync(kConsumerThreads);
-        const uint32_t r0 = static_cast<uint32_t>(row0);
+        const uint32_t r0 = static_cast<uint32_t>(row0 + p.vocab_off);  // global token ids
         block_select_topk(
             nrows, p.topk, [&](int i) { return topk_key(lg[i], r0 + static_cast<uint32_t>(i)); }, outk, sel, tid,
             kConsumerThreads, [] { consumer_sync(kConsumerThreads); });
-        uint64_t *dst = p.cand_key + (static_cast<int64_t>(b) * G + blockIdx.x) * kMaxTopK;
-        for (int j = tid; j < p.topk; j += kConsumerThreads) dst[j] = outk[j];
+        if (p.tp > 1) {  // to every rank's candidate block [tp][xB][G][kMaxTopK], slot of this rank
+            const int64_t off = ((static_cast<int64_t>(p.tp_rank) * p.xB + b) * G + blockIdx.x) * kMaxTopK;
+            for (int r = 0; r < p.tp; ++r) {
+                uint64_t *dst = reinterpret_cast<uint64_t *>(p.xpeer[r] + p.x_cand) + off;
+                for (int j = tid; j < p.topk; j += kConsumerThreads) dst[j] = outk[j];
+            }
+        } else {
+            uint64_t *dst = p.cand_key + (static_cast<int64_t>(b) * G + blockIdx.x) * kMaxTopK;
+            for (int j = tid; j < p.topk; j += kConsumerThreads) dst[j] = outk[j];
+        }
         consumer_sync(kConsumerThreads);
     }
 }
@@ -879,13 +952,22 @@ static __device__ __noinline__ int32_t row_draw(const DecodeParams &p, const Sme
     uint64_t *outk = reinterpret_cast<uint64_t *>(after);
     double *fscr = reinterpret_cast<double *>(after + kMaxTopK * sizeof(uint64_t));
     int *oscr = reinterpret_cast<int *>(fscr + kMaxTopK);
-    const uint64_t *ck = p.cand_key + static_cast<int64_t>(b) * G * kMaxTopK;
+    // candidates (rank s, CTA g, k): tp = 1 reads this rank's cand_key; tp > 1
+    // the exchange block that every rank wrote its CTAs' candidates into
+    const uint64_t *ck = p.tp > 1 ? reinterpret_cast<const uint64_t *>(p.xpeer[p.tp_rank] + p.x_cand) +
+                                        static_cast<int64_t>(b) * G * kMaxTopK
+                                  : p.cand_key + static_cast<int64_t>(b) * G * kMaxTopK;
+    const int64_t sstride = static_cast<int64_t>(p.xB) * G * kMaxTopK;
     const int K = p.topk;
-    const int n = G * K;
+    const int GK = G * K;
+    const int n = p.tp * GK;
+    auto cand_at = [&](int i) {
+        const int s = i / GK, r = i - s * GK;
+        return __ldcg(ck + s * sstride + (r / K) * kMaxTopK + (r % K));
+    };
     if (static_cast<size_t>(n) * sizeof(uint64_t) > static_cast<size_t>(p.S) * kStageBytes) {  // ring too small
         block_select_topk(
-            n, K, [&](int i) { return __ldcg(ck + (i / K) * kMaxTopK + (i % K)); }, outk, sel, tid, kConsumerThreads,
-            [] { consumer_sync(kConsumerThreads); });
+            n, K, cand_at, outk, sel, tid, kConsumerThreads, [] { consumer_sync(kConsumerThreads); });
     } else {
     uint64_t *keys = reinterpret_cast<uint64_t *>(sm.ring);
     for (int i0 = 0; i0 < n; i0 += 16 * kConsumerThreads) {
@@ -893,7 +975,7 @@ static __device__ __noinline__ int32_t row_draw(const DecodeParams &p, const Sme
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             const int i = i0 + tid + j * kConsumerThreads;
-            v[j] = i < n ? __ldcg(ck + (i / K) * kMaxTopK + (i % K)) : 0ull;
+            v[j] = i < n ? cand_at(i) : 0ull;
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -914,7 +996,7 @@ static __device__ __noinline__ int32_t row_draw(const DecodeParams &p, const Sme
 }
 
 // ---------------------------------------------------------------- consumer phases
-template <typename WT, int NB>
+template <typename WT, int NB, bool TP>
 __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &ss, int tid) {
     const int G = gridDim.x;
     constexpr int B = NB;
@@ -941,9 +1023,16 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                 const LayerPtrs &prev = sm.layers[layer - 1];
                 NormW nw;
                 norm_prefetch(nw, prev.post_ff_ln, lp.in_ln, p.H, tid);
-                if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
                 // x = r + norm(mlp, post_ff) (layers.mojo:216-220), xs = norm(x, input_layernorm) (195)
-                stage_norm<NB>(p.r, p.mlp_raw, prev.post_ff_ln, lp.in_ln, nw, out_h, p.H, p.inv_h, g.Kp, sm.xs, ss, tid);
+                if constexpr (TP) {  // mlp = the sum of every rank's down_proj partial of layer - 1
+                    ok = xwait(p, 1, p.xep + layer - 1, 100 + ph, ss, tid) && ok;
+                    stage_norm<NB, true>(p.r, xrecv(p, p.tp_rank, 1), prev.post_ff_ln, lp.in_ln, nw, out_h, p.H,
+                                         p.inv_h, g.Kp, sm.xs, ss, tid, p.tp, static_cast<int64_t>(p.xB) * p.H);
+                } else {
+                    if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+                    stage_norm<NB>(p.r, p.mlp_raw, prev.post_ff_ln, lp.in_ln, nw, out_h, p.H, p.inv_h, g.Kp, sm.xs,
+                                   ss, tid);
+                }
             }
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                              GemvOut{p.qkv, p.qkv_rows});
@@ -964,18 +1053,27 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             if (has_dep)
                 ok = cta_wait(ctr_phase(p, ph - 1), static_cast<uint32_t>(a.nitems), p.err, 100 + ph, ss, tid) && ok;
             att_combine(p, a, g.Kp, sm.xs, tid);
+            // with tensor parallelism the row-split o_proj partials go to every rank
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                             GemvOut{p.o_raw, p.H});
+                                 TP ? GemvOut{nullptr, p.H, ss.xdst_o, p.tp} : GemvOut{p.o_raw, p.H});
             cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+            if constexpr (TP) xsignal(p, 0, tid);
         } else if (kind == PH_GU) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
             NormW nw;
             norm_prefetch(nw, lp.post_attn_ln, lp.pre_ff_ln, p.H, tid);
-            if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
             // r = h + norm(o_raw, post_attn) (layers.mojo:202-207); xs = norm(r, pre_ff) (209-210)
-            stage_norm<NB>(p.h, p.o_raw, lp.post_attn_ln, lp.pre_ff_ln, nw, blockIdx.x == 0 ? p.r : nullptr, p.H,
-                           p.inv_h, g.Kp, sm.xs, ss, tid);
+            if constexpr (TP) {  // o_raw = the sum of every rank's o_proj partial
+                ok = xwait(p, 0, p.xep + layer, 100 + ph, ss, tid) && ok;
+                stage_norm<NB, true>(p.h, xrecv(p, p.tp_rank, 0), lp.post_attn_ln, lp.pre_ff_ln, nw,
+                                     blockIdx.x == 0 ? p.r : nullptr, p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.tp,
+                                     static_cast<int64_t>(p.xB) * p.H);
+            } else {
+                if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+                stage_norm<NB>(p.h, p.o_raw, lp.post_attn_ln, lp.pre_ff_ln, nw, blockIdx.x == 0 ? p.r : nullptr,
+                               p.H, p.inv_h, g.Kp, sm.xs, ss, tid);
+            }
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                              GemvOut{p.act, p.Ip});
             cta_signal(ctr_phase(p, ph), 1u, ss, tid);
@@ -1002,18 +1100,25 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             }
             consumer_sync(kConsumerThreads);
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                             GemvOut{p.mlp_raw, p.H});
+                                 TP ? GemvOut{nullptr, p.H, ss.xdst_d, p.tp} : GemvOut{p.mlp_raw, p.H});
             cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+            if constexpr (TP) xsignal(p, 1, tid);
         } else if (kind == PH_LMH) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
             if (p.lm_mode != kLmNone) {
                 NormW nw;
                 norm_prefetch(nw, lp.post_ff_ln, p.final_norm, p.H, tid);
-                if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
                 // x = r + norm(mlp_raw, post_ff); xs = norm(x, final norm) (layers.mojo:283-285)
-                stage_norm<NB>(p.r, p.mlp_raw, lp.post_ff_ln, p.final_norm, nw, nullptr, p.H, p.inv_h, g.Kp, sm.xs, ss,
-                               tid);
+                if constexpr (TP) {
+                    ok = xwait(p, 1, p.xep + p.L - 1, 100 + ph, ss, tid) && ok;
+                    stage_norm<NB, true>(p.r, xrecv(p, p.tp_rank, 1), lp.post_ff_ln, p.final_norm, nw, nullptr,
+                                         p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.tp, static_cast<int64_t>(p.xB) * p.H);
+                } else {
+                    if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+                    stage_norm<NB>(p.r, p.mlp_raw, lp.post_ff_ln, p.final_norm, nw, nullptr, p.H, p.inv_h, g.Kp,
+                                   sm.xs, ss, tid);
+                }
             }
             if (p.lm_mode == kLmEmbed) {
                 if (blockIdx.x == 0 && ok)
@@ -1030,11 +1135,17 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                 }
             }
             cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+            // every rank's logits and candidates are complete once this exchange is counted
+            if constexpr (TP)
+                if (p.lm_mode == kLmLogits) xsignal(p, 2, tid);
         } else {  // PH_SAMPLE
             const int b = blockIdx.x;
             if (b < B) {
                 int32_t token = -1;
-                if (p.sample && p.lm_mode == kLmLogits && p.topk > 0) {
+                if constexpr (TP) {
+                    if (p.lm_mode == kLmLogits) ok = xwait(p, 2, p.lm_ep, 100 + ph, ss, tid) && ok;
+                    if (p.sample && p.lm_mode == kLmLogits && p.topk > 0) token = row_draw(p, sm, b, ok, tid);
+                } else if (p.sample && p.lm_mode == kLmLogits && p.topk > 0) {
                     if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
                     token = row_draw(p, sm, b, ok, tid);
                 }
@@ -1142,7 +1253,7 @@ __device__ void producer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
 }
 
 // ---------------------------------------------------------------- the kernel
-template <typename WT, int NB>
+template <typename WT, int NB, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ SmallSmem ss;
@@ -1188,7 +1299,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         } else {
             tok = p.tok[b];
         }
-        if (tok < 0 || tok >= p.V) {
+        if (tok < 0 || tok >= p.V_full) {
             set_error(p.err, kErrBadToken | static_cast<uint32_t>(b));
             tok = 0;
         }
@@ -1201,6 +1312,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         ss.pos[b] = pos;
         ss.tok[b] = tok;
         ss.active[b] = active;
+    }
+    if (TP && tid == 0) {  // this rank's receive block on every rank
+        for (int r = 0; r < p.tp; ++r) {
+            const int64_t blk = static_cast<int64_t>(p.tp_rank) * p.xB * p.H;
+            ss.xdst_o[r] = xrecv(p, r, 0) + blk;
+            ss.xdst_d[r] = xrecv(p, r, 1) + blk;
+        }
     }
     __syncthreads();
     uint64_t *tr_kernel =
@@ -1215,7 +1333,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     if ((tid >> 5) == kConsumerWarps) {
         if ((tid & 31) == 0) producer_run<WT, NB>(p, sm, ss);
     } else {
-        consumer_run<WT, NB>(p, sm, ss, tid);
+        consumer_run<WT, NB, TP>(p, sm, ss, tid);
     }
 
     // ---- exit: the last CTA out resets the counters used by this launch.
@@ -1239,39 +1357,47 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 // Static shared memory of the kernel (SmallSmem and the pointer block) in bytes.
 template <typename WT, int NB>
 size_t decode_static_smem_nb() {
+    size_t m = 0;
     cudaFuncAttributes a;
-    if (cudaFuncGetAttributes(&a, decode_kernel<WT, NB>) != cudaSuccess) return 1024;
-    return a.sharedSizeBytes;
+    if (cudaFuncGetAttributes(&a, decode_kernel<WT, NB, false>) != cudaSuccess) return 2048;
+    m = a.sharedSizeBytes;
+    if (cudaFuncGetAttributes(&a, decode_kernel<WT, NB, true>) != cudaSuccess) return 2048;
+    return m > a.sharedSizeBytes ? m : a.sharedSizeBytes;
 }
 
 template <typename WT, int NB>
 cudaError_t decode_prepare_nb(size_t dynamic_smem) {
-    return cudaFuncSetAttribute(decode_kernel<WT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<WT, NB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(dynamic_smem));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(decode_kernel<WT, NB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(dynamic_smem));
 }
 
 template <typename WT, int NB>
 int decode_occupancy_nb(size_t smem) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<WT, NB>, kThreads, smem) != cudaSuccess)
+    int n0 = 0, n1 = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n0, decode_kernel<WT, NB, false>, kThreads, smem) !=
+        cudaSuccess)
         return 0;
-    return n;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n1, decode_kernel<WT, NB, true>, kThreads, smem) !=
+        cudaSuccess)
+        return 0;
+    return n0 < n1 ? n0 : n1;
 }
 
 template <typename WT, int NB>
 cudaError_t decode_launch_nb(const DecodeParams &p, int grid, size_t smem, cudaStream_t stream, bool cooperative) {
-    if (cooperative) {
-        void *args[] = {const_cast<DecodeParams *>(&p)};
-        return cudaLaunchCooperativeKernel(reinterpret_cast<void *>(decode_kernel<WT, NB>), dim3(grid),
-                                           dim3(kThreads), args, smem, stream);
-    }
-    decode_kernel<WT, NB><<<grid, kThreads, smem, stream>>>(p);
-    return cudaGetLastError();
+    void *fn = p.tp > 1 ? reinterpret_cast<void *>(decode_kernel<WT, NB, true>)
+                        : reinterpret_cast<void *>(decode_kernel<WT, NB, false>);
+    void *args[] = {const_cast<DecodeParams *>(&p)};
+    if (cooperative) return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kThreads), args, smem, stream);
+    return cudaLaunchKernel(fn, dim3(grid), dim3(kThreads), args, smem, stream);
 }
 
 }  // namespace mg
 
-// Explicit instantiation of the host helpers (and so of the kernel) for one row count.
+// Explicit instantiation of the host helpers (and so of the kernels) for one row count.
 #define MG_DECODE_INSTANTIATE_WT(WT, NB)                                                                       \
     namespace mg {                                                                                             \
     template size_t decode_static_smem_nb<WT, NB>();                                                           \

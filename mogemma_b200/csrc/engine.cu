@@ -114,6 +114,17 @@ struct mg_model {
     bool trace_on = false;
     int max_inflight = 2;       // outstanding bulk copies per CTA (MOGEMMA_B200_INFLIGHT)
     int pf_tiles = 0;           // L2 prefetch distance in tiles (MOGEMMA_B200_PREFETCH)
+
+    // tensor parallelism: Hq, Hkv, A, I, V above are this rank's shard; *_g the model's
+    int tp = 1, tp_rank = 0;
+    int Hq_g = 0, Hkv_g = 0, I_g = 0, V_g = 0, v0 = 0;
+    char *xbuf = nullptr;                  // exchange buffer (IPC-shared with the other ranks)
+    size_t x_cnt = 0, x_o = 0, x_d = 0, x_cand = 0, x_logits = 0;
+    char *xpeer[kMaxTp] = {};              // every rank's exchange buffer (own at tp_rank)
+    std::vector<void *> ipc_open;          // peer mappings to close
+    bool tp_connected = false;
+    uint64_t x_ep = 0, lm_ep = 0;          // exchanges of earlier forwards (same on every rank)
+    float *logits_full = nullptr;          // [Bmax][V_g] gathered logits (tp > 1)
 };
 
 template <typename T>
@@ -156,7 +167,33 @@ struct Desc {
     const void *data = nullptr;
     std::vector<int64_t> shape;
     int dtype = MG_F32;
+    int64_t ld = 0;  // host row stride in elements (0: the tensor's own width)
 };
+
+// Rows [row0, ...) of a [rows, cols] tensor, and columns [col0, ...) (a strided
+// view: rows keep the tensor's stride).  A tensor-parallel rank uploads its
+// shard through these.
+static Desc rows_view(const Desc &d, int64_t row0) {
+    Desc v = d;
+    const int64_t w = d.ld ? d.ld : (d.shape.size() > 1 ? d.shape[1] : 1);
+    v.data = static_cast<const char *>(d.data) + row0 * w * static_cast<int64_t>(dsize(d.dtype));
+    return v;
+}
+static Desc cols_view(const Desc &d, int64_t col0) {
+    Desc v = d;
+    v.ld = d.ld ? d.ld : d.shape[1];
+    v.data = static_cast<const char *>(d.data) + col0 * static_cast<int64_t>(dsize(d.dtype));
+    return v;
+}
+
+// Host rows [r0, r0 + nr) of d (width cols) into contiguous staging memory.
+static cudaError_t stage_rows(mg_model *m, const Desc &d, int64_t r0, int64_t nr, int64_t cols, void *staging) {
+    const size_t es = dsize(d.dtype);
+    const int64_t w = d.ld ? d.ld : cols;
+    const char *src = static_cast<const char *>(d.data) + r0 * w * static_cast<int64_t>(es);
+    if (w == cols) return cudaMemcpyAsync(staging, src, nr * cols * es, cudaMemcpyHostToDevice, m->stream);
+    return cudaMemcpy2DAsync(staging, cols * es, src, w * es, cols * es, nr, cudaMemcpyHostToDevice, m->stream);
+}
 
 static const Desc *find(const std::map<std::string, Desc> &d, const std::string &name) {
     auto it = d.find(name);
@@ -173,8 +210,7 @@ static mg_status upload_matrix(mg_model *m, const Desc &d, int64_t rows, int64_t
     const int64_t rows_per = std::max<int64_t>(1, static_cast<int64_t>(staging_bytes / std::max<size_t>(row_bytes, 1)));
     for (int64_t r0 = 0; r0 < rows; r0 += rows_per) {
         const int64_t nr = std::min(rows_per, rows - r0);
-        CU(cudaMemcpyAsync(staging, static_cast<const char *>(d.data) + r0 * row_bytes, nr * row_bytes,
-                           cudaMemcpyHostToDevice, m->stream));
+        CU(stage_rows(m, d, r0, nr, cols, staging));
         CU(convert_rows_launch(staging, d.dtype, nr, cols, static_cast<char *>(dst) + r0 * dst_ld * dsize(dst_dtype),
                                dst_dtype, dst_ld, m->stream));
     }
@@ -193,8 +229,7 @@ static mg_status upload_tiled(mg_model *m, const Desc &d, int64_t rows, int64_t 
     const int64_t rows_per = std::max<int64_t>(1, static_cast<int64_t>(staging_bytes / std::max<size_t>(row_bytes, 1)));
     for (int64_t r0 = 0; r0 < rows; r0 += rows_per) {
         const int64_t nr = std::min(rows_per, rows - r0);
-        CU(cudaMemcpyAsync(staging, static_cast<const char *>(d.data) + r0 * row_bytes, nr * row_bytes,
-                           cudaMemcpyHostToDevice, m->stream));
+        CU(stage_rows(m, d, r0, nr, cols, staging));
         CU(tile_rows_launch(staging, d.dtype, nr, cols, row_off + r0, dst, dst_dtype, Kp, sh.rps, sh.mult, sh.kc,
                             sh.nseg, part, m->stream));
     }
@@ -205,6 +240,7 @@ static mg_status destroy_impl(mg_model *m) {
     if (!m) return MG_OK;
     cudaSetDevice(m->dev);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    for (void *p : m->ipc_open) cudaIpcCloseMemHandle(p);
     for (void *p : m->allocs) cudaFree(p);
     if (m->pinned) cudaFreeHost(m->pinned);
     if (m->own_stream && m->stream) cudaStreamDestroy(m->stream);
@@ -241,7 +277,11 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     m->cap = opt && opt->capacity > 0 ? opt->capacity : 8192;
     m->seed = opt ? opt->seed : 0;
     m->decode_path = opt ? opt->decode_path : 0;
-    if (opt && opt->tp_size > 1) return fail(MG_ERR_UNSUPPORTED, "tensor parallelism is not built into this library");
+    m->tp = opt && opt->tp_size > 1 ? opt->tp_size : 1;
+    m->tp_rank = m->tp > 1 ? opt->tp_rank : 0;
+    if (m->tp > kMaxTp || m->tp_rank < 0 || m->tp_rank >= m->tp)
+        return fail(MG_ERR_INVALID, "tensor-parallel rank %d of %d outside [0, tp) or tp > %d", m->tp_rank, m->tp,
+                    kMaxTp);
 
     // ---- dimensions (init_model_mojo, core.mojo:316-325)
     const Desc *emb = find(d, "model.embed_tokens.weight");
@@ -313,6 +353,41 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         if (kn) TRY(need(kn, hd, 0, p + "self_attn.k_norm.weight"));
     }
 
+    // ---- tensor-parallel shard: q heads, the kv heads they use, FFN rows and
+    // vocabulary rows of this rank; o_proj and down_proj are split along their
+    // input (columns) so their outputs are partial sums exchanged in the kernel
+    m->Hq_g = m->Hq;
+    m->Hkv_g = m->Hkv;
+    m->I_g = m->I;
+    m->V_g = m->V;
+    int qh0 = 0, kvh0 = 0, i0 = 0;
+    if (m->tp > 1) {
+        const int T = m->tp, r = m->tp_rank, Gq_g = m->Hq / m->Hkv;
+        if (m->Hq % T != 0 || m->I % T != 0 || m->V % T != 0)
+            return fail(MG_ERR_UNSUPPORTED, "tp=%d must divide the q heads (%d), intermediate size (%d) and vocabulary (%d)",
+                        T, m->Hq, m->I, m->V);
+        const int hq_r = m->Hq / T;
+        qh0 = r * hq_r;
+        if (m->Hkv % T == 0) {
+            m->Hkv = m->Hkv / T;
+            kvh0 = r * m->Hkv;
+        } else if (Gq_g % hq_r == 0) {  // fewer kv heads than ranks: each rank keeps the one its q heads use
+            m->Hkv = 1;
+            kvh0 = qh0 / Gq_g;
+        } else {
+            return fail(MG_ERR_UNSUPPORTED, "tp=%d does not split %d q heads over %d kv heads", T, m->Hq, m->Hkv_g);
+        }
+        m->Hq = hq_r;
+        m->I = m->I / T;
+        i0 = r * m->I;
+        m->V = m->V / T;
+        m->v0 = r * m->V;
+        m->A = m->Hq * hd;
+        m->Ap = static_cast<int>(pad128(m->A));
+        m->Ip = static_cast<int>(pad128(m->I));
+        m->qkv_rows = m->A + 2 * m->Hkv * hd;
+    }
+
     // ---- launch geometry
     CU(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->dev));
     int max_smem = 0;
@@ -373,20 +448,20 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         TRY(dalloc(m, reinterpret_cast<char **>(&gu), static_cast<size_t>(tiled_elems(sh_gu, m->I)) * we));
         TRY(dalloc(m, reinterpret_cast<char **>(&down), static_cast<size_t>(tiled_elems(sh_i, m->H)) * we));
         const int64_t kvr = static_cast<int64_t>(m->Hkv) * hd;
-        TRY(upload_tiled(m, *lw(l, "self_attn.q_proj.weight"), m->A, m->H, 0, qkv, wd, m->Hp, sh_h, 0, staging,
-                         staging_bytes));
-        TRY(upload_tiled(m, *lw(l, "self_attn.k_proj.weight"), kvr, m->H, m->A, qkv, wd, m->Hp, sh_h, 0, staging,
-                         staging_bytes));
-        TRY(upload_tiled(m, *lw(l, "self_attn.v_proj.weight"), kvr, m->H, m->A + kvr, qkv, wd, m->Hp, sh_h, 0,
+        TRY(upload_tiled(m, rows_view(*lw(l, "self_attn.q_proj.weight"), static_cast<int64_t>(qh0) * hd), m->A,
+                         m->H, 0, qkv, wd, m->Hp, sh_h, 0, staging, staging_bytes));
+        TRY(upload_tiled(m, rows_view(*lw(l, "self_attn.k_proj.weight"), static_cast<int64_t>(kvh0) * hd), kvr,
+                         m->H, m->A, qkv, wd, m->Hp, sh_h, 0, staging, staging_bytes));
+        TRY(upload_tiled(m, rows_view(*lw(l, "self_attn.v_proj.weight"), static_cast<int64_t>(kvh0) * hd), kvr,
+                         m->H, m->A + kvr, qkv, wd, m->Hp, sh_h, 0, staging, staging_bytes));
+        TRY(upload_tiled(m, cols_view(*lw(l, "self_attn.o_proj.weight"), static_cast<int64_t>(qh0) * hd), m->H,
+                         m->A, 0, o, wd, m->Ap, sh_a, 0, staging, staging_bytes));
+        TRY(upload_tiled(m, rows_view(*lw(l, "mlp.gate_proj.weight"), i0), m->I, m->H, 0, gu, wd, m->Hp, sh_gu, 0,
                          staging, staging_bytes));
-        TRY(upload_tiled(m, *lw(l, "self_attn.o_proj.weight"), m->H, m->A, 0, o, wd, m->Ap, sh_a, 0, staging,
-                         staging_bytes));
-        TRY(upload_tiled(m, *lw(l, "mlp.gate_proj.weight"), m->I, m->H, 0, gu, wd, m->Hp, sh_gu, 0, staging,
-                         staging_bytes));
-        TRY(upload_tiled(m, *lw(l, "mlp.up_proj.weight"), m->I, m->H, 0, gu, wd, m->Hp, sh_gu, 1, staging,
-                         staging_bytes));
-        TRY(upload_tiled(m, *lw(l, "mlp.down_proj.weight"), m->H, m->I, 0, down, wd, m->Ip, sh_i, 0, staging,
-                         staging_bytes));
+        TRY(upload_tiled(m, rows_view(*lw(l, "mlp.up_proj.weight"), i0), m->I, m->H, 0, gu, wd, m->Hp, sh_gu, 1,
+                         staging, staging_bytes));
+        TRY(upload_tiled(m, cols_view(*lw(l, "mlp.down_proj.weight"), i0), m->H, m->I, 0, down, wd, m->Ip, sh_i, 0,
+                         staging, staging_bytes));
         void *gate = gu, *up = nullptr;
         m->weight_bytes += static_cast<int64_t>(we) * (static_cast<int64_t>(m->qkv_rows) * m->H +
                                                         static_cast<int64_t>(m->H) * m->A +
@@ -421,12 +496,13 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         lp.is_global = (m->mode == 0) ? 1 : (((l + 1) % m->global_every) == 0 ? 1 : 0);
     }
     TRY(dalloc(m, reinterpret_cast<char **>(&m->lm_head), static_cast<size_t>(tiled_elems(sh_h, m->V)) * we));
-    TRY(upload_tiled(m, *lmh, m->V, m->H, 0, m->lm_head, wd, m->Hp, sh_h, 0, staging, staging_bytes));
+    TRY(upload_tiled(m, rows_view(*lmh, m->v0), m->V, m->H, 0, m->lm_head, wd, m->Hp, sh_h, 0, staging,
+                     staging_bytes));
     m->weight_bytes += static_cast<int64_t>(we) * m->V * m->H;
     // embedding rows are gathered, so they stay row-major (a separate copy even
     // when lm_head is tied to them, convert.py:129-131)
-    TRY(dalloc(m, reinterpret_cast<char **>(&m->embed), static_cast<size_t>(m->V) * m->H * we));
-    TRY(upload_matrix(m, *emb, m->V, m->H, m->embed, wd, m->H, staging, staging_bytes));
+    TRY(dalloc(m, reinterpret_cast<char **>(&m->embed), static_cast<size_t>(m->V_g) * m->H * we));
+    TRY(upload_matrix(m, *emb, m->V_g, m->H, m->embed, wd, m->H, staging, staging_bytes));
     m->embed_ld = m->H;
     TRY(dalloc(m, &m->final_norm, m->H));
     TRY(upload_matrix(m, *fnorm, 1, m->H, m->final_norm, MG_F32, m->H, staging, staging_bytes));
@@ -469,7 +545,27 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     TRY(dalloc(m, &m->mlp_raw, static_cast<size_t>(B) * m->H));
     TRY(dalloc(m, &m->attn_part, static_cast<size_t>(B) * m->Hkv * m->max_ch * Gq * (hd + kPartHead)));
     TRY(dalloc(m, &m->attn_out, static_cast<size_t>(B) * m->Ap));
-    TRY(dalloc(m, &m->logits, static_cast<size_t>(B) * m->V));
+    if (m->tp > 1) {
+        // exchange buffer: counters, o_proj / down_proj partials [tp][Bmax][H],
+        // lm_head candidates [tp][Bmax][G][kMaxTopK], this rank's logits [Bmax][V]
+        size_t off = 0;
+        auto take = [&](size_t bytes) {
+            const size_t o = off;
+            off = (off + bytes + 255) / 256 * 256;
+            return o;
+        };
+        const size_t T = static_cast<size_t>(m->tp);
+        m->x_cnt = take(4 * sizeof(uint64_t));
+        m->x_o = take(T * B * m->H * sizeof(float));
+        m->x_d = take(T * B * m->H * sizeof(float));
+        m->x_cand = take(T * B * m->G * kMaxTopK * sizeof(uint64_t));
+        m->x_logits = take(static_cast<size_t>(B) * m->V * sizeof(float));
+        TRY(dalloc(m, &m->xbuf, off));
+        m->logits = reinterpret_cast<float *>(m->xbuf + m->x_logits);
+        TRY(dalloc(m, &m->logits_full, static_cast<size_t>(B) * m->V_g));
+    } else {
+        TRY(dalloc(m, &m->logits, static_cast<size_t>(B) * m->V));
+    }
     TRY(dalloc(m, &m->emb_acc, static_cast<size_t>(B) * m->H));
     TRY(dalloc(m, &m->cand_key, static_cast<size_t>(B) * m->G * kMaxTopK));
     TRY(dalloc(m, &m->tok, kMaxRows));
@@ -505,17 +601,17 @@ extern "C" mg_status mg_model_create(const mg_tensor_desc *descs, int32_t n, con
 extern "C" mg_status mg_model_info_get(const mg_model *m, mg_model_info *info) {
     if (!m || !info) return fail(MG_ERR_INVALID, "null argument");
     info->num_layers = m->L;
-    info->num_heads = m->Hq;
-    info->num_kv_heads = m->Hkv;
+    info->num_heads = m->Hq_g;
+    info->num_kv_heads = m->Hkv_g;
     info->head_dim = m->hd;
     info->hidden_size = m->H;
-    info->intermediate_size = m->I;
-    info->vocab_size = m->V;
+    info->intermediate_size = m->I_g;
+    info->vocab_size = m->V_g;
     info->max_seq_len = m->cap;
     info->max_batch = m->Bmax;
     info->mode = m->mode;
     info->weight_dtype = m->wdtype;
-    info->tp_size = 1;
+    info->tp_size = m->tp;
     info->weight_bytes_per_step = m->weight_bytes;
     info->kv_bytes_per_pos = static_cast<int64_t>(2) * m->L * m->Hkv * m->hd * 4;
     info->num_sms = m->num_sms;
@@ -586,6 +682,18 @@ static DecodeParams base_params(mg_model *m, int B) {
     p.n_phases = num_phases(m->L);
     p.ph_begin = 0;
     p.ph_end = p.n_phases;
+    p.V_full = m->V_g;
+    p.tp = m->tp;
+    p.tp_rank = m->tp_rank;
+    p.vocab_off = m->v0;
+    p.xB = m->Bmax;
+    p.xep = m->x_ep;
+    p.lm_ep = m->lm_ep;
+    for (int r = 0; r < m->tp && m->tp > 1; ++r) p.xpeer[r] = m->xpeer[r];
+    p.x_cnt = static_cast<int64_t>(m->x_cnt);
+    p.x_o = static_cast<int64_t>(m->x_o);
+    p.x_d = static_cast<int64_t>(m->x_d);
+    p.x_cand = static_cast<int64_t>(m->x_cand);
     return p;
 }
 
@@ -599,6 +707,8 @@ static int att_chunk(const mg_model *m, int B, int max_ctx) {
 }
 
 static mg_status run_decode(mg_model *m, DecodeParams &p, int max_ctx) {
+    if (m->tp > 1 && !m->tp_connected)
+        return fail(MG_ERR_INVALID, "tensor-parallel model used before mg_tp_connect");
     p.att_ch = att_chunk(m, p.B, max_ctx);
     const bool persistent = m->decode_path == 0;
     if (persistent) {
@@ -615,6 +725,20 @@ static mg_status run_decode(mg_model *m, DecodeParams &p, int max_ctx) {
             if (e != cudaSuccess) return fail(MG_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
         }
     }
+    // every rank runs the same forwards, so these stay equal across ranks
+    m->x_ep += static_cast<uint64_t>(m->L);
+    if (p.lm_mode == kLmLogits) m->lm_ep += 1;
+    return MG_OK;
+}
+
+// tp > 1: every rank's logits slice into logits_full [B][V_g] (after the
+// launch, whose last phase waited for all ranks' lm_head).
+static mg_status gather_logits(mg_model *m, int batch) {
+    const size_t row = static_cast<size_t>(m->V) * sizeof(float);
+    for (int r = 0; r < m->tp; ++r)
+        for (int b = 0; b < batch; ++b)
+            CU(cudaMemcpyAsync(m->logits_full + static_cast<size_t>(b) * m->V_g + static_cast<size_t>(r) * m->V,
+                               m->xpeer[r] + m->x_logits + b * row, row, cudaMemcpyDeviceToDevice, m->stream));
     return MG_OK;
 }
 
@@ -647,11 +771,11 @@ static SampleCfg sample_cfg(const mg_model *m, const mg_sampling *s) {
     if (s->temperature <= 0.0) {
         c.topk = 1;
         c.fused = true;
-    } else if (s->top_k > 0 && s->top_k < m->V && s->top_k <= kMaxTopK) {
+    } else if (s->top_k > 0 && s->top_k < m->V_g && s->top_k <= kMaxTopK) {
         c.topk = s->top_k;
         c.fused = true;
-    } else if (m->V <= kMaxTopK) {
-        c.topk = m->V;
+    } else if (m->V_g <= kMaxTopK && m->tp == 1) {
+        c.topk = m->V_g;
         c.fused = true;
     } else {
         c.general = true;
@@ -689,14 +813,19 @@ static mg_status step_impl(mg_model *m, int batch, float *logits_host, int32_t *
     int max_ctx = 0;
     for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, m->h_pos[b] + 1);
     TRY(run_decode(m, p, max_ctx));
+    float *logits = m->logits;
+    if (m->tp > 1 && (sc.general || logits_host)) {
+        TRY(gather_logits(m, batch));
+        logits = m->logits_full;
+    }
     if (sc.general) {
-        CU(sample_rows_launch(m->logits, m->V, batch, m->V, s->temperature, s->top_k, s->top_p, p.uniforms, m->seed,
+        CU(sample_rows_launch(logits, m->V_g, batch, m->V_g, s->temperature, s->top_k, s->top_p, p.uniforms, m->seed,
                               m->rng_offset, nullptr, m->tok, m->stream));
     }
     if (s) m->rng_offset += 1;
     for (int b = 0; b < batch; ++b) m->h_pos[b] += 1;
     if (logits_host)
-        CU(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * batch * m->V, cudaMemcpyDeviceToHost, m->stream));
+        CU(cudaMemcpyAsync(logits_host, logits, sizeof(float) * batch * m->V_g, cudaMemcpyDeviceToHost, m->stream));
     if (sampled_host && s) {
         CU(cudaMemcpyAsync(m->pinned, m->tok, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, m->stream));
     }
@@ -718,8 +847,8 @@ extern "C" mg_status mg_step(mg_model *m, const int32_t *token_ids_host, int32_t
     TRY(validate_rows(m, batch));
     CU(cudaSetDevice(m->dev));
     for (int b = 0; b < batch; ++b)
-        if (token_ids_host[b] < 0 || token_ids_host[b] >= m->V)
-            return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", token_ids_host[b], m->V);
+        if (token_ids_host[b] < 0 || token_ids_host[b] >= m->V_g)
+            return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", token_ids_host[b], m->V_g);
     memcpy(m->pinned, token_ids_host, sizeof(int32_t) * batch);
     CU(cudaMemcpyAsync(m->tok, m->pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, m->stream));
     return step_impl(m, batch, logits_host, sampled_host, s, true);
@@ -730,8 +859,8 @@ extern "C" mg_status mg_set_tokens(mg_model *m, const int32_t *token_ids_host, i
     TRY(validate_rows(m, batch));
     CU(cudaSetDevice(m->dev));
     for (int b = 0; b < batch; ++b)
-        if (token_ids_host[b] < 0 || token_ids_host[b] >= m->V)
-            return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", token_ids_host[b], m->V);
+        if (token_ids_host[b] < 0 || token_ids_host[b] >= m->V_g)
+            return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", token_ids_host[b], m->V_g);
     CU(cudaMemcpyAsync(m->tok, token_ids_host, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, m->stream));
     CU(cudaStreamSynchronize(m->stream));
     return MG_OK;
@@ -767,9 +896,15 @@ extern "C" mg_status mg_generate(mg_model *m, int32_t n_steps, int32_t batch, co
         int max_ctx = 0;
         for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, m->h_pos[b] + 1);
         TRY(run_decode(m, p, max_ctx));
-        if (sc.general)
-            CU(sample_rows_launch(m->logits, m->V, batch, m->V, s->temperature, s->top_k, s->top_p, nullptr, m->seed,
+        if (sc.general) {
+            float *logits = m->logits;
+            if (m->tp > 1) {
+                TRY(gather_logits(m, batch));
+                logits = m->logits_full;
+            }
+            CU(sample_rows_launch(logits, m->V_g, batch, m->V_g, s->temperature, s->top_k, s->top_p, nullptr, m->seed,
                                   m->rng_offset, p.out_tokens, m->tok, m->stream));
+        }
         m->rng_offset += 1;
         for (int b = 0; b < batch; ++b) m->h_pos[b] += 1;
     }
@@ -796,7 +931,7 @@ static mg_status upload_ids(mg_model *m, const int32_t *ids, const int32_t *lens
         if (lens[b] < 0 || lens[b] > max_len) return fail(MG_ERR_INVALID, "row %d length %d outside [0, %d]", b, lens[b], max_len);
         for (int t = 0; t < lens[b]; ++t) {
             const int32_t id = ids[static_cast<int64_t>(b) * max_len + t];
-            if (id < 0 || id >= m->V) return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", id, m->V);
+            if (id < 0 || id >= m->V_g) return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", id, m->V_g);
         }
     }
     CU(cudaMemcpyAsync(m->ids, ids, sizeof(int32_t) * need, cudaMemcpyHostToDevice, m->stream));
@@ -961,7 +1096,46 @@ extern "C" mg_status mg_trace_read(mg_model *m, uint64_t *out_host, int64_t capa
     return MG_OK;
 }
 
-extern "C" mg_status mg_nccl_unique_id(void *out128) {
-    (void)out128;
-    return fail(MG_ERR_UNSUPPORTED, "tensor parallelism is not built into this library");
+extern "C" mg_status mg_tp_ipc_handle(const mg_model *m, void *out) {
+    if (!m || !out) return fail(MG_ERR_INVALID, "null argument");
+    if (m->tp < 2) return fail(MG_ERR_INVALID, "model is not tensor-parallel");
+    static_assert(sizeof(cudaIpcMemHandle_t) == MG_TP_HANDLE_BYTES, "IPC handle size");
+    CU(cudaSetDevice(m->dev));
+    cudaIpcMemHandle_t h;
+    CU(cudaIpcGetMemHandle(&h, m->xbuf));
+    memcpy(out, &h, sizeof h);
+    return MG_OK;
+}
+
+extern "C" mg_status mg_tp_connect(mg_model *m, const void *handles, int32_t n) {
+    if (!m || !handles) return fail(MG_ERR_INVALID, "null argument");
+    if (m->tp < 2) return fail(MG_ERR_INVALID, "model is not tensor-parallel");
+    if (n != m->tp) return fail(MG_ERR_INVALID, "%d handles given for tp=%d", n, m->tp);
+    if (m->tp_connected) return fail(MG_ERR_INVALID, "already connected");
+    CU(cudaSetDevice(m->dev));
+    for (int r = 0; r < m->tp; ++r) {
+        if (r == m->tp_rank) {
+            m->xpeer[r] = m->xbuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char *>(handles) + static_cast<size_t>(r) * MG_TP_HANDLE_BYTES, sizeof h);
+        void *ptr = nullptr;
+        CU(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        m->ipc_open.push_back(ptr);
+        m->xpeer[r] = static_cast<char *>(ptr);
+    }
+    m->tp_connected = true;
+    return MG_OK;
+}
+
+extern "C" mg_status mg_tp_disconnect(mg_model *m) {
+    if (!m) return fail(MG_ERR_INVALID, "null model");
+    CU(cudaSetDevice(m->dev));
+    if (m->stream) CU(cudaStreamSynchronize(m->stream));
+    for (void *p : m->ipc_open) CU(cudaIpcCloseMemHandle(p));
+    m->ipc_open.clear();
+    for (int r = 0; r < kMaxTp; ++r) m->xpeer[r] = nullptr;
+    m->tp_connected = false;
+    return MG_OK;
 }

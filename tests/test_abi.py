@@ -40,7 +40,7 @@ def test_struct_layout_matches_header(tmp_path: Path) -> None:
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "mogemma_b200.h"\n'
         "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(mg_tensor_desc), sizeof(mg_options),"
-        " sizeof(mg_model_info), sizeof(mg_sampling), offsetof(mg_options, seed), offsetof(mg_options, nccl_id),"
+        " sizeof(mg_model_info), sizeof(mg_sampling), offsetof(mg_options, seed), offsetof(mg_options, reserved1),"
         " offsetof(mg_sampling, uniforms_host)); return 0;}\n")
     exe = tmp_path / "sizes"
     try:
@@ -51,7 +51,7 @@ def test_struct_layout_matches_header(tmp_path: Path) -> None:
     import ctypes  # noqa: PLC0415
 
     want = [ctypes.sizeof(_core.TensorDesc), ctypes.sizeof(_core.Options), ctypes.sizeof(_core.ModelInfo),
-            ctypes.sizeof(_core.Sampling), _core.Options.seed.offset, _core.Options.nccl_id.offset,
+            ctypes.sizeof(_core.Sampling), _core.Options.seed.offset, _core.Options.reserved1.offset,
             _core.Sampling.uniforms_host.offset]
     assert got == want
 
