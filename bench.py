@@ -94,12 +94,14 @@ class ClockSampler:
 
 
 def algorithmic_bytes(info, pos0: int, n: int) -> float:
-    """Average bytes one decode-kernel launch must move for positions pos0..pos0+n-1."""
-    kv_row = 2 * info.num_kv_heads * info.head_dim * 4  # K+V fp32, one layer, one position
+    """Average bytes one decode-kernel launch (of one rank) must move for positions pos0..pos0+n-1."""
+    tp = max(1, int(info.tp_size))
+    kv_heads = info.num_kv_heads // tp if info.num_kv_heads % tp == 0 else 1  # this rank's kv heads
+    kv_row = 2 * kv_heads * info.head_dim * 4  # K+V fp32, one layer, one position
     ctx_avg = pos0 + (n + 1) / 2.0
     kv_read = info.num_layers * kv_row * ctx_avg
     kv_write = info.num_layers * kv_row
-    logits = info.vocab_size * 4
+    logits = info.vocab_size // tp * 4
     emb_row = info.hidden_size * (4 if info.weight_dtype == 0 else 2)
     return float(info.weight_bytes_per_step + kv_read + kv_write + logits + emb_row)
 
@@ -219,6 +221,8 @@ def main() -> None:
     ap.add_argument("--model", default=CONFIG, help="synthetic config (gemma3-270m for small profiling runs)")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled before the timed decode")
     ap.add_argument("--decode", type=int, default=DECODE, help="tokens decoded per step")
+    ap.add_argument("--parallel", default="replicas", choices=["replicas", "tp"],
+                    help="N>1: independent replicas (weak scaling) or one tensor-parallel model over the N GPUs")
     args = ap.parse_args()
     CONFIG, PROMPT, DECODE = args.model, args.prompt, args.decode
     world, rank, local = dist_setup()
@@ -234,8 +238,13 @@ def main() -> None:
 
     d = synth.CONFIGS[CONFIG]
     weights = synth.make_weights(d, seed=0, bf16=args.weight_dtype == "bf16")
-    llm = _core.init_model(synth.metadata_of(weights), device=local, capacity=PROMPT + DECODE, max_batch=1,
-                           weight_dtype=args.weight_dtype, seed=1234 + rank)
+    tp = args.parallel == "tp" and world > 1
+    if tp:  # every rank holds its shard; the same seed on every rank draws the same tokens
+        llm = _core.init_model_tp(synth.metadata_of(weights), device=local, capacity=PROMPT + DECODE, max_batch=1,
+                                  weight_dtype=args.weight_dtype, seed=1234)
+    else:
+        llm = _core.init_model(synth.metadata_of(weights), device=local, capacity=PROMPT + DECODE, max_batch=1,
+                               weight_dtype=args.weight_dtype, seed=1234 + rank)
     h = llm["_handle"]
     info = h.info
     lib = _core.lib()
@@ -267,7 +276,8 @@ def main() -> None:
         barrier(world)
     ms = ev0.elapsed_time(ev1)
     ms = dist_max(ms, world)
-    tokens = args.steps * DECODE * world
+    streams = 1 if tp else world
+    tokens = args.steps * DECODE * streams
     value = tokens / (ms / 1000.0)
     ms_launch = ms / (args.steps * DECODE)
     bytes_launch = algorithmic_bytes(info, PROMPT - 1, DECODE)
@@ -293,7 +303,7 @@ def main() -> None:
     for _ in range(e2e_steps):
         e2e_step()
     e2e_s = dist_max(time.perf_counter() - t0, world)
-    e2e_value = e2e_steps * DECODE * world / e2e_s
+    e2e_value = e2e_steps * DECODE * streams / e2e_s
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -301,13 +311,14 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": args.weight_dtype,
             "data": "synthetic (seeded N(0,0.02) random-init weights, uniform random prompt ids)",
             "config": {"workload": f"{CONFIG} batch-1 decode: {PROMPT}-token prompt then {DECODE} tokens "
                                    f"(T={TEMPERATURE}, top-k {TOP_K}), {args.weight_dtype} weights",
-                       "model": CONFIG, "global_batch": world, "seq_len": PROMPT + DECODE,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "model": CONFIG, "global_batch": streams, "seq_len": PROMPT + DECODE,
+                       "parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1 else "single GPU",
                        "l2": f"inputs larger than L2 ({info.weight_bytes_per_step / 1e9:.2f} GB of weights per token)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * DECODE,
                     "d2h_bytes_per_step": 4 * DECODE},
@@ -324,7 +335,10 @@ def main() -> None:
             "ms_per_token": ms_launch,
         }
         print(json.dumps(line), flush=True)
-    h.close()
+    if tp:
+        _core.close_tp(llm)
+    else:
+        h.close()
     if world > 1:
         import torch.distributed as dist  # noqa: PLC0415
 
