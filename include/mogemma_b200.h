@@ -202,6 +202,17 @@ mg_status mg_trace_read(mg_model *m, uint64_t *out_host, int64_t capacity, int64
 #define MG_TP_HANDLE_BYTES 64
 mg_status mg_tp_ipc_handle(const mg_model *m, void *out /* MG_TP_HANDLE_BYTES */);
 mg_status mg_tp_connect(mg_model *m, const void *handles /* n * MG_TP_HANDLE_BYTES, rank order */, int32_t n);
+/* ---- tensor-core GEMM (no counterpart in the reference: its projections are
+ * one-token vec_mat_mul, ops.mojo:69-95; this is the dense contraction of the
+ * batched prefill path) ----
+ * C[M][N] (fp32, row stride ldc) = A[M][K] . B[N][K]^T with A and B bf16 device
+ * matrices (row strides lda, ldb; rows 16-byte aligned), K a multiple of 64, on
+ * tcgen05 tensor cores with fp32 accumulation.  err_dev is a device word that
+ * receives a nonzero code if a bounded wait inside the kernel expires.
+ * Asynchronous on `stream` (a cudaStream_t; NULL: the legacy default stream). */
+mg_status mg_gemm_bf16(const void *a_dev, int64_t lda, const void *b_dev, int64_t ldb, float *c_dev, int64_t ldc,
+                       int32_t M, int32_t N, int32_t K, uint32_t *err_dev, void *stream);
+
 /* Unmaps the other ranks' buffers.  Every rank calls it (after its last step)
  * before any rank destroys its model, so no buffer is freed while mapped. */
 mg_status mg_tp_disconnect(mg_model *m);

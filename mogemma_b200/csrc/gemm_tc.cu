@@ -1,0 +1,237 @@
+// gemm_tc.cu -- tcgen05 tensor-core GEMM, the dense contraction of the batched
+// (prefill) path: C[M][N] (fp32) = A[M][K] (bf16) . B[N][K]^T (bf16), both
+// operands K-major (activations [tokens][features], weights [out][in] as the
+// reference stores them, convert.py:92-121).
+//
+// One CTA computes a 128 x 128 tile of C with 4 warps:
+//  * warp 0, one lane: TMA producer -- 2-D tiled bulk tensor loads of a
+//    128 x 64 A tile and a 128 x 64 B tile per stage (128-byte swizzle) into a
+//    4-stage ring, completing on the stage's mbarrier;
+//  * warp 1: allocates 128 TMEM columns (the fp32 accumulator, 128 lanes x 128
+//    columns); one lane issues tcgen05.mma (M=128, N=128, K=16, bf16 -> f32) four
+//    times per stage from shared-memory descriptors, and tcgen05.commit releases
+//    the stage once the MMAs have read it;
+//  * all 4 warps: epilogue -- warp w reads TMEM lanes 32w..32w+31 (rows of the
+//    tile) with tcgen05.ld and stores them to C.
+// Every mbarrier wait is bounded (common.cuh); on expiry the kernel records an
+// error code, skips the rest of the work, frees its TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/mogemma_b200.h"
+#include "common.cuh"
+
+namespace mg {
+mg_status report_error(mg_status st, const char *msg);
+
+namespace tc {
+constexpr int kBM = 128;   // tile rows (TMEM lanes)
+constexpr int kBN = 128;   // tile columns (TMEM columns)
+constexpr int kBK = 64;    // K per stage: 64 bf16 = 128 bytes, one swizzle row
+constexpr int kUK = 16;    // K of one tcgen05.mma (kind::f16)
+constexpr int kStages = 4;
+constexpr int kThreads = 128;
+constexpr uint32_t kABytes = kBM * kBK * 2;
+constexpr uint32_t kBBytes = kBN * kBK * 2;
+constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * (kABytes + kBBytes);
+constexpr uint32_t kTmemCols = 128;
+constexpr uint32_t kErrTcFull = 0x21000000u, kErrTcEmpty = 0x22000000u, kErrTcDone = 0x23000000u;
+
+// Instruction descriptor (kind::f16): D f32 (bits 4-5 = 1), A bf16 (7-9 = 1),
+// B bf16 (10-12 = 1), both K-major (15, 16 = 0), N >> 3 at 17-22, M >> 4 at 24-28.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(kBN) >> 3) << 17) |
+                            ((static_cast<uint32_t>(kBM) >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle
+// layout that the TMA writes: rows 128 bytes apart, 8-row groups 1024 bytes
+// apart (stride byte offset), descriptor version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %4, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(kIdesc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        float *C, int M, int N, int K, int64_t ldc, uint32_t *err) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full[kStages], empty[kStages], done;
+    __shared__ uint32_t tmem_slot;
+    const uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
+    const uint32_t sa = smem_u32(reinterpret_cast<void *>(base));
+    const uint32_t sb = sa + kStages * kABytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+    const int nk = K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        for (int kt = 0; kt < nk; ++kt) {
+            const int s = kt % kStages;
+            if (kt >= kStages && !mbar_wait(&empty[s], ((kt / kStages) - 1) & 1u, err, kErrTcEmpty)) break;
+            mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+            tma_load_2d(sa + s * kABytes, &map_a, kt * kBK, m0, smem_u32(&full[s]));
+            tma_load_2d(sb + s * kBBytes, &map_b, kt * kBK, n0, smem_u32(&full[s]));
+        }
+    } else if (warp == 1 && lane == 0) {
+        for (int kt = 0; kt < nk; ++kt) {
+            const int s = kt % kStages;
+            if (!mbar_wait(&full[s], (kt / kStages) & 1u, err, kErrTcFull)) break;
+            tc_fence_after();
+            const uint32_t a0 = sa + s * kABytes, b0 = sb + s * kBBytes;
+#pragma unroll
+            for (int k = 0; k < kBK / kUK; ++k)
+                umma_bf16(tmem, sw128_desc(a0 + k * kUK * 2), sw128_desc(b0 + k * kUK * 2), (kt | k) != 0 ? 1u : 0u);
+            umma_commit(smem_u32(&empty[s]));
+        }
+        umma_commit(smem_u32(&done));  // arrives once every MMA issued above has completed
+    }
+    __syncwarp();
+
+    // epilogue: warp w owns TMEM lanes (tile rows) 32w .. 32w + 31
+    const bool have = mbar_wait(&done, 0u, err, kErrTcDone);
+    tc_fence_after();
+    const int row = m0 + warp * 32 + lane;
+    // tcgen05.ld is warp-collective: decide per warp
+    if (__all_sync(0xffffffffu, have && ld_relaxed_u32(err) == 0u)) {
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(c0), v);
+            if (row < M) {
+                float *dst = C + static_cast<int64_t>(row) * ldc + n0 + c0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (n0 + c0 + j < N) dst[j] = __uint_as_float(v[j]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// ---------------------------------------------------------------- host
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// [rows][K] bf16 with row stride ld elements; boxes of 64 x box_rows, 128-byte swizzle.
+static bool make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, int64_t ld, int box_rows) {
+    EncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace tc
+
+// C[M][N] = A[M][K] . B[N][K]^T; A, B bf16 device memory (16-byte aligned rows),
+// K a multiple of 64, err a device word that receives a code on a timeout.
+cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb, float *C, int64_t ldc, int M, int N,
+                         int K, uint32_t *err, cudaStream_t stream) {
+    using namespace tc;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kSmem));
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, A, M, K, lda, kBM) || !make_map(&mb, B, N, K, ldb, kBN)) return cudaErrorInvalidValue;
+    const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
+    gemm_bf16_tc_kernel<<<grid, kThreads, kSmem, stream>>>(ma, mb, C, M, N, K, ldc, err);
+    return cudaGetLastError();
+}
+
+}  // namespace mg
+
+using namespace mg;
+
+extern "C" mg_status mg_gemm_bf16(const void *a_dev, int64_t lda, const void *b_dev, int64_t ldb, float *c_dev,
+                                  int64_t ldc, int32_t M, int32_t N, int32_t K, uint32_t *err_dev, void *stream) {
+    if (!a_dev || !b_dev || !c_dev || !err_dev) return report_error(MG_ERR_INVALID, "mg_gemm_bf16: null pointer");
+    if (M <= 0 || N <= 0 || K <= 0 || K % tc::kBK != 0)
+        return report_error(MG_ERR_INVALID, "mg_gemm_bf16: need M, N > 0 and K a positive multiple of 64");
+    if (lda < K || ldb < K || ldc < N || (lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(a_dev) % 16 != 0 || reinterpret_cast<uintptr_t>(b_dev) % 16 != 0)
+        return report_error(MG_ERR_INVALID, "mg_gemm_bf16: rows must be 16-byte aligned and strides >= extents");
+    const cudaError_t e = gemm_bf16_tc(a_dev, lda, b_dev, ldb, c_dev, ldc, M, N, K, err_dev,
+                                       static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        char buf[160];
+        snprintf(buf, sizeof buf, "mg_gemm_bf16: %s", cudaGetErrorString(e));
+        return report_error(MG_ERR_CUDA, buf);
+    }
+    return MG_OK;
+}
