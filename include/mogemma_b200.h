@@ -84,7 +84,9 @@ typedef struct mg_options {
     int32_t decode_path;      /* 0: persistent decode kernel; 1: one launch per phase */
     int32_t tp_rank;          /* tensor-parallel rank (0 when tp_size == 1) */
     int32_t tp_size;          /* tensor-parallel degree (1..8); one process per GPU, see mg_tp_connect */
-    int32_t reserved0;
+    int32_t prefill_path;     /* 0: mg_prefill feeds tokens one step at a time through the decode kernel (the
+                                 reference's arithmetic); 1: all prompt tokens per layer at once, projections
+                                 as tcgen05 GEMMs on bf16-rounded inputs (tp_size 1) */
     const void *reserved1;
 } mg_options;
 

@@ -76,7 +76,7 @@ class Options(ctypes.Structure):
         ("decode_path", ctypes.c_int32),
         ("tp_rank", ctypes.c_int32),
         ("tp_size", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("prefill_path", ctypes.c_int32),
         ("reserved1", ctypes.c_void_p),
     ]
 
@@ -277,6 +277,7 @@ def create_model(metadata: dict[str, Any], **options: Any) -> ModelHandle:
     o.seed = int(options.get("seed", _env_int("MOGEMMA_B200_SEED", 0))) & 0xFFFFFFFFFFFFFFFF
     o.stream = options.get("stream")
     o.decode_path = int(options.get("decode_path", _env_int("MOGEMMA_B200_DECODE_PATH", 0)))
+    o.prefill_path = int(options.get("prefill_path", _env_int("MOGEMMA_B200_PREFILL", 0)))
     o.tp_rank = int(options.get("tp_rank", 0))
     o.tp_size = int(options.get("tp_size", 1))
     out = _P()

@@ -34,6 +34,21 @@ cudaError_t sample_rows_launch(const float *logits, int64_t ld, int rows, int V,
                                int32_t *tok, cudaStream_t stream);
 cudaError_t convert_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, void *dst, int dst_dtype,
                                 int64_t dst_ld, cudaStream_t stream);
+cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb, float *C, int64_t ldc, int M, int N,
+                         int K, uint32_t *err, cudaStream_t stream);
+cudaError_t pf_embed(const void *E, int wdtype_bf16, int64_t ld, const int32_t *tok, int N, int H, float scale,
+                     float *x, cudaStream_t s);
+cudaError_t pf_resnorm(const float *base, const float *add, const float *w_add, const float *w_next, float *res,
+                       __nv_bfloat16 *xn, int N, int H, int Kp, float inv_h, cudaStream_t s);
+cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *q_norm,
+                          const float *k_norm, const float *cos_t, const float *sin_t, const int32_t *row,
+                          const int32_t *pos, float *kc, float *vc, int64_t kv_row_stride, int64_t kv_head_stride,
+                          float inv_hd, cudaStream_t s);
+cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,
+                         const float *vc, const int32_t *row, const int32_t *pos, int64_t kv_row_stride,
+                         int64_t kv_head_stride, int window, int is_global, float scale, __nv_bfloat16 *out,
+                         int out_ld, cudaStream_t s);
+cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, cudaStream_t s);
 cudaError_t tile_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, int64_t row_off, void *dst,
                              int dst_dtype, int Kp, int rps, int mult, int kc, int nseg, int part,
                              cudaStream_t stream);
@@ -125,6 +140,18 @@ struct mg_model {
     bool tp_connected = false;
     uint64_t x_ep = 0, lm_ep = 0;          // exchanges of earlier forwards (same on every rank)
     float *logits_full = nullptr;          // [Bmax][V_g] gathered logits (tp > 1)
+
+    // batched prefill (prefill_path 1): bf16 row-major projection weights for
+    // the tensor-core GEMMs and a workspace for pf_cap packed tokens
+    int prefill_path = 0;
+    struct PfLayer {
+        __nv_bfloat16 *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+    };
+    std::vector<PfLayer> pf;
+    int pf_cap = 0, pf_kx = 0, pf_cx = 0;
+    float *pf_x = nullptr, *pf_r = nullptr, *pf_c = nullptr;
+    __nv_bfloat16 *pf_xn = nullptr;
+    int32_t *pf_tok = nullptr, *pf_row = nullptr, *pf_pos = nullptr;
 };
 
 template <typename T>
@@ -277,6 +304,8 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     m->cap = opt && opt->capacity > 0 ? opt->capacity : 8192;
     m->seed = opt ? opt->seed : 0;
     m->decode_path = opt ? opt->decode_path : 0;
+    m->prefill_path = opt ? opt->prefill_path : 0;
+    if (const char *e = getenv("MOGEMMA_B200_PREFILL")) m->prefill_path = atoi(e);
     m->tp = opt && opt->tp_size > 1 ? opt->tp_size : 1;
     m->tp_rank = m->tp > 1 ? opt->tp_rank : 0;
     if (m->tp > kMaxTp || m->tp_rank < 0 || m->tp_rank >= m->tp)
@@ -494,6 +523,28 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         lp.q_norm = norms[4];
         lp.k_norm = norms[5];
         lp.is_global = (m->mode == 0) ? 1 : (((l + 1) % m->global_every) == 0 ? 1 : 0);
+        if (m->prefill_path == 1 && m->tp == 1) {  // row-major bf16 copies for the prefill GEMMs
+            mg_model::PfLayer pl;
+            TRY(dalloc(m, &pl.qkv, static_cast<size_t>(m->qkv_rows) * m->Hp));
+            TRY(dalloc(m, &pl.o, static_cast<size_t>(m->H) * m->Ap));
+            TRY(dalloc(m, &pl.gu, static_cast<size_t>(2) * m->I * m->Hp));
+            TRY(dalloc(m, &pl.down, static_cast<size_t>(m->H) * m->Ip));
+            TRY(upload_matrix(m, *lw(l, "self_attn.q_proj.weight"), m->A, m->H, pl.qkv, MG_BF16, m->Hp, staging,
+                              staging_bytes));
+            TRY(upload_matrix(m, *lw(l, "self_attn.k_proj.weight"), kvr, m->H, pl.qkv + static_cast<size_t>(m->A) * m->Hp,
+                              MG_BF16, m->Hp, staging, staging_bytes));
+            TRY(upload_matrix(m, *lw(l, "self_attn.v_proj.weight"), kvr, m->H,
+                              pl.qkv + static_cast<size_t>(m->A + kvr) * m->Hp, MG_BF16, m->Hp, staging, staging_bytes));
+            TRY(upload_matrix(m, *lw(l, "self_attn.o_proj.weight"), m->H, m->A, pl.o, MG_BF16, m->Ap, staging,
+                              staging_bytes));
+            TRY(upload_matrix(m, *lw(l, "mlp.gate_proj.weight"), m->I, m->H, pl.gu, MG_BF16, m->Hp, staging,
+                              staging_bytes));
+            TRY(upload_matrix(m, *lw(l, "mlp.up_proj.weight"), m->I, m->H, pl.gu + static_cast<size_t>(m->I) * m->Hp,
+                              MG_BF16, m->Hp, staging, staging_bytes));
+            TRY(upload_matrix(m, *lw(l, "mlp.down_proj.weight"), m->H, m->I, pl.down, MG_BF16, m->Ip, staging,
+                              staging_bytes));
+            m->pf.push_back(pl);
+        }
     }
     TRY(dalloc(m, reinterpret_cast<char **>(&m->lm_head), static_cast<size_t>(tiled_elems(sh_h, m->V)) * we));
     TRY(upload_tiled(m, rows_view(*lmh, m->v0), m->V, m->H, 0, m->lm_head, wd, m->Hp, sh_h, 0, staging,
@@ -939,6 +990,68 @@ static mg_status upload_ids(mg_model *m, const int32_t *ids, const int32_t *lens
     return MG_OK;
 }
 
+// Batched prefill (prefill_path 1): all prompt tokens of all rows per layer,
+// projections on the tensor cores (prefill.cu, gemm_tc.cu).
+static mg_status prefill_batched(mg_model *m, const int32_t *ids, const int32_t *lens, int batch, int max_len) {
+    std::vector<int32_t> tok, row, pos;
+    for (int b = 0; b < batch; ++b)
+        for (int t = 0; t < lens[b]; ++t) {
+            tok.push_back(ids[static_cast<int64_t>(b) * max_len + t]);
+            row.push_back(b);
+            pos.push_back(m->h_pos[b] + t);
+        }
+    const int N = static_cast<int>(tok.size());
+    if (N == 0) return MG_OK;
+    if (N > m->pf_cap) {  // workspace for N packed tokens (kept for later calls)
+        const int cap = std::max(N, 256);
+        m->pf_kx = std::max(m->Hp, std::max(m->Ap, m->Ip));
+        m->pf_cx = std::max(m->qkv_rows, std::max(m->H, 2 * m->I));
+        TRY(dalloc(m, &m->pf_x, static_cast<size_t>(cap) * m->H));
+        TRY(dalloc(m, &m->pf_r, static_cast<size_t>(cap) * m->H));
+        TRY(dalloc(m, &m->pf_c, static_cast<size_t>(cap) * m->pf_cx));
+        TRY(dalloc(m, &m->pf_xn, static_cast<size_t>(cap) * m->pf_kx));
+        TRY(dalloc(m, &m->pf_tok, cap));
+        TRY(dalloc(m, &m->pf_row, cap));
+        TRY(dalloc(m, &m->pf_pos, cap));
+        m->pf_cap = cap;
+    }
+    cudaStream_t st = m->stream;
+    CU(cudaMemcpyAsync(m->pf_tok, tok.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+    CU(cudaMemcpyAsync(m->pf_row, row.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+    CU(cudaMemcpyAsync(m->pf_pos, pos.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+    const float inv_h = 1.0f / static_cast<float>(m->H), inv_hd = 1.0f / static_cast<float>(m->hd);
+    const float att_scale = 1.0f / sqrtf(static_cast<float>(m->hd));
+    CU(pf_embed(m->embed, m->wdtype == MG_BF16, m->embed_ld, m->pf_tok, N, m->H, sqrtf(static_cast<float>(m->H)),
+                m->pf_x, st));
+    CU(pf_resnorm(m->pf_x, nullptr, nullptr, m->h_layers[0].in_ln, m->pf_x, m->pf_xn, N, m->H, m->Hp, inv_h, st));
+    auto gemm = [&](const __nv_bfloat16 *a, int lda, const __nv_bfloat16 *w, int n_out, int K, float *c,
+                    int ldc) -> mg_status {
+        CU(gemm_bf16_tc(a, lda, w, K, c, ldc, N, n_out, K, m->err, st));
+        return MG_OK;
+    };
+    for (int l = 0; l < m->L; ++l) {
+        const LayerPtrs &lp = m->h_layers[l];
+        const mg_model::PfLayer &w = m->pf[l];
+        float *kc = m->kc + static_cast<int64_t>(l) * m->kv_layer_stride;
+        float *vc = m->vc + static_cast<int64_t>(l) * m->kv_layer_stride;
+        TRY(gemm(m->pf_xn, m->Hp, w.qkv, m->qkv_rows, m->Hp, m->pf_c, m->qkv_rows));
+        CU(pf_qk_rope_kv(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, lp.q_norm, lp.k_norm,
+                         lp.is_global ? m->cos_g : m->cos_l, lp.is_global ? m->sin_g : m->sin_l, m->pf_row, m->pf_pos,
+                         kc, vc, m->kv_row_stride, m->kv_head_stride, inv_hd, st));
+        if (m->Ap > m->A) CU(cudaMemsetAsync(m->pf_xn, 0, sizeof(__nv_bfloat16) * N * m->Ap, st));
+        CU(pf_attention(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, kc, vc, m->pf_row, m->pf_pos,
+                        m->kv_row_stride, m->kv_head_stride, m->window, lp.is_global, att_scale, m->pf_xn, m->Ap, st));
+        TRY(gemm(m->pf_xn, m->Ap, w.o, m->H, m->Ap, m->pf_c, m->H));
+        CU(pf_resnorm(m->pf_x, m->pf_c, lp.post_attn_ln, lp.pre_ff_ln, m->pf_r, m->pf_xn, N, m->H, m->Hp, inv_h, st));
+        TRY(gemm(m->pf_xn, m->Hp, w.gu, 2 * m->I, m->Hp, m->pf_c, 2 * m->I));
+        CU(pf_geglu(m->pf_c, m->I, 2 * m->I, m->pf_xn, m->Ip, N, st));
+        TRY(gemm(m->pf_xn, m->Ip, w.down, m->H, m->Ip, m->pf_c, m->H));
+        const float *w_next = l + 1 < m->L ? m->h_layers[l + 1].in_ln : m->final_norm;
+        CU(pf_resnorm(m->pf_r, m->pf_c, lp.post_ff_ln, w_next, m->pf_x, m->pf_xn, N, m->H, m->Hp, inv_h, st));
+    }
+    return MG_OK;
+}
+
 extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
                                 int32_t max_len) {
     if (!m || !token_ids_host || !lens_host) return fail(MG_ERR_INVALID, "null argument");
@@ -952,6 +1065,20 @@ extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, cons
     if (longest == 0) return MG_OK;
     TRY(upload_ids(m, token_ids_host, lens_host, batch, max_len));
     std::vector<int32_t> pos0 = m->h_pos;
+    if (m->prefill_path == 1 && m->tp == 1) {
+        mg_status st = prefill_batched(m, token_ids_host, lens_host, batch, max_len);
+        if (st == MG_OK) {
+            for (int b = 0; b < batch; ++b) m->h_pos[b] = pos0[b] + lens_host[b];
+            CU(cudaMemcpyAsync(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice,
+                               m->stream));
+            st = check_device(m);
+        }
+        if (st != MG_OK) {
+            m->h_pos = pos0;
+            CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+        }
+        return st;
+    }
     for (int t = 0; t < longest; ++t) {
         DecodeParams p = base_params(m, batch);
         p.lm_mode = kLmNone;

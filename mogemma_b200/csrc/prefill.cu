@@ -1,0 +1,232 @@
+// prefill.cu -- the batched prefill path: every prompt token of every row in
+// one pass per layer, with the projections as tcgen05 GEMMs (gemm_tc.cu) and
+// these kernels around them.  Same arithmetic as the decode kernel apart from
+// the projections, whose inputs are rounded to bf16 for the tensor cores.
+//
+// Per layer, for the N packed tokens (row b(n), position pos(n)):
+//   xn  = bf16(rmsnorm(x) (1 + in_ln))                      pf_resnorm
+//   qkv = xn . Wqkv^T                                       GEMM
+//   QK-norm + RoPE of q and k, k and v into the KV cache    pf_qk_rope_kv
+//   a   = bf16(causal softmax(q k^T / sqrt(hd)) v)          pf_attention
+//   o   = a . Wo^T                                          GEMM
+//   r   = x + rmsnorm(o) (1 + post_attn); xn = bf16(rmsnorm(r) (1 + pre_ff))   pf_resnorm
+//   gu  = xn . [Wgate; Wup]^T                               GEMM
+//   act = bf16(gelu_erf(g) u)                               pf_geglu
+//   m   = act . Wdown^T                                     GEMM
+//   x   = r + rmsnorm(m) (1 + post_ff)  (and the next layer's xn)             pf_resnorm
+// (layers.mojo:174-220 for the layer, 16-97 attention, 101-118 MLP.)
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.cuh"
+#include "decode.cuh"
+
+namespace mg {
+
+constexpr int kPfThreads = 256;
+
+__device__ __forceinline__ float block_sum_pf(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kPfThreads / 32; ++w) t += red[w];
+    return t;
+}
+
+// x = E[tok] * sqrt(H) (model.mojo:62-68, layers.mojo:247-251)
+template <typename ET>
+__global__ void __launch_bounds__(kPfThreads) pf_embed_kernel(const ET *E, int64_t ld, const int32_t *tok, int H,
+                                                              float scale, float *x) {
+    const int n = blockIdx.x;
+    const ET *e = E + static_cast<int64_t>(tok[n]) * ld;
+    for (int i = threadIdx.x; i < H; i += kPfThreads) x[static_cast<int64_t>(n) * H + i] = ld_w(e + i) * scale;
+}
+
+// res = base + (add ? rmsnorm(add) (1 + w_add) : 0);  xn = bf16(rmsnorm(res) (1 + w_next)), zero padded to Kp.
+// res may alias base.  One CTA per token.
+__global__ void __launch_bounds__(kPfThreads) pf_resnorm_kernel(const float *base, const float *add,
+                                                                const float *w_add, const float *w_next, float *res,
+                                                                __nv_bfloat16 *xn, int H, int Kp, float inv_h) {
+    __shared__ float red[kPfThreads / 32];
+    const int64_t n = blockIdx.x;
+    const float *b = base + n * H;
+    float inv_a = 0.f;
+    if (add) {
+        float s = 0.f;
+        for (int i = threadIdx.x; i < H; i += kPfThreads) {
+            const float v = add[n * H + i];
+            s += v * v;
+        }
+        inv_a = rms_inv(block_sum_pf(s, red), inv_h);
+    }
+    float s2 = 0.f;
+    for (int i = threadIdx.x; i < H; i += kPfThreads) {
+        float x = b[i];
+        if (add) x += add[n * H + i] * inv_a * (1.0f + w_add[i]);
+        res[n * H + i] = x;
+        s2 += x * x;
+    }
+    const float inv = rms_inv(block_sum_pf(s2, red), inv_h);
+    for (int i = threadIdx.x; i < Kp; i += kPfThreads)
+        xn[n * Kp + i] = __float2bfloat16_rn(i < H ? res[n * H + i] * inv * (1.0f + w_next[i]) : 0.f);
+}
+
+// QK-norm (layers.mojo:43-49) and RoPE (52-55) of each token's q heads (in
+// place) and k head(s); k and v into the KV cache at (row, pos) (57-61).
+// One CTA per token, one warp per head vector.
+__global__ void __launch_bounds__(kPfThreads) pf_qk_rope_kv_kernel(
+    float *qkv, int qkv_ld, int Hq, int Hkv, int hd, int hdp, const float *q_norm, const float *k_norm,
+    const float *cos_t, const float *sin_t, const int32_t *row, const int32_t *pos, float *kc, float *vc,
+    int64_t kv_row_stride, int64_t kv_head_stride, float inv_hd) {
+    const int64_t n = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int half = hd / 2;
+    const int p = pos[n];
+    float *x0 = qkv + n * qkv_ld;
+    for (int vec = warp; vec < Hq + Hkv; vec += kPfThreads / 32) {
+        float *x = x0 + static_cast<int64_t>(vec) * hd;  // q heads then k heads (layout of the qkv rows)
+        const float *nw = vec < Hq ? q_norm : k_norm;
+        if (nw) {
+            float s = 0.f;
+            for (int d = lane; d < hd; d += 32) s += x[d] * x[d];
+            const float inv = rms_inv(warp_sum(s), inv_hd);
+            for (int d = lane; d < hd; d += 32) x[d] = x[d] * inv * (1.0f + nw[d]);
+            __syncwarp();
+        }
+        const float *c = cos_t + static_cast<int64_t>(p) * half;
+        const float *sn = sin_t + static_cast<int64_t>(p) * half;
+        for (int i = lane; i < half; i += 32) {
+            const float x1 = x[i], x2 = x[i + half];
+            x[i] = x1 * c[i] - x2 * sn[i];
+            x[i + half] = x2 * c[i] + x1 * sn[i];
+        }
+        __syncwarp();
+        if (vec >= Hq) {
+            const int kvh = vec - Hq;
+            const int64_t off = row[n] * kv_row_stride + kvh * kv_head_stride + static_cast<int64_t>(p) * hdp;
+            const float *v = x0 + static_cast<int64_t>(Hq + Hkv + kvh) * hd;
+            for (int d = lane; d < hd; d += 32) {
+                kc[off + d] = x[d];
+                vc[off + d] = v[d];
+            }
+        }
+    }
+}
+
+// Causal attention of one (token, q head) per warp over the cached positions
+// lo..pos (layers.mojo:63-94): online softmax, lanes over head dims.  The
+// cache already holds every prompt key of this layer.
+__global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
+    const float *qkv, int qkv_ld, int Hq, int Hkv, int hd, int hdp, const float *kc, const float *vc,
+    const int32_t *row, const int32_t *pos, int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global,
+    float scale, __nv_bfloat16 *out, int out_ld, int N) {
+    constexpr int kDL = kMaxHeadDim / 32;
+    const int lane = threadIdx.x & 31;
+    const int64_t task = static_cast<int64_t>(blockIdx.x) * (kPfThreads / 32) + (threadIdx.x >> 5);
+    if (task >= static_cast<int64_t>(N) * Hq) return;
+    const int64_t n = task / Hq;
+    const int h = static_cast<int>(task - n * Hq);
+    const int kvh = h / (Hq / Hkv);
+    const int p = pos[n];
+    const int lo = (!is_global && window > 0 && p - window + 1 > 0) ? p - window + 1 : 0;
+    const float *q = qkv + n * qkv_ld + static_cast<int64_t>(h) * hd;
+    float qr[kDL], acc[kDL];
+#pragma unroll
+    for (int i = 0; i < kDL; ++i) {
+        const int d = lane + 32 * i;
+        qr[i] = d < hd ? q[d] : 0.f;
+        acc[i] = 0.f;
+    }
+    const float *kb = kc + row[n] * kv_row_stride + kvh * kv_head_stride;
+    const float *vb = vc + row[n] * kv_row_stride + kvh * kv_head_stride;
+    float m = -INFINITY, l = 0.f;
+    for (int t = lo; t <= p; ++t) {
+        const float *k = kb + static_cast<int64_t>(t) * hdp;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < kDL; ++i) {
+            const int d = lane + 32 * i;
+            if (d < hd) s += qr[i] * k[d];
+        }
+        s = warp_sum(s) * scale;
+        const float m_new = fmaxf(m, s);
+        const float alpha = (m == -INFINITY) ? 0.f : expf(m - m_new);
+        const float e = expf(s - m_new);
+        l = l * alpha + e;
+        const float *v = vb + static_cast<int64_t>(t) * hdp;
+#pragma unroll
+        for (int i = 0; i < kDL; ++i) {
+            const int d = lane + 32 * i;
+            if (d < hd) acc[i] = acc[i] * alpha + e * v[d];
+        }
+        m = m_new;
+    }
+    const float inv_l = 1.0f / l;
+    __nv_bfloat16 *o = out + n * out_ld + static_cast<int64_t>(h) * hd;
+#pragma unroll
+    for (int i = 0; i < kDL; ++i) {
+        const int d = lane + 32 * i;
+        if (d < hd) o[d] = __float2bfloat16_rn(acc[i] * inv_l);
+    }
+}
+
+// act = bf16(gelu_erf(gate) * up) (ops.mojo:5-30); gu rows hold [gate (I) | up (I)].
+__global__ void __launch_bounds__(kPfThreads) pf_geglu_kernel(const float *gu, int I, int gu_ld, __nv_bfloat16 *act,
+                                                              int Ip) {
+    const int64_t n = blockIdx.y;
+    for (int i = blockIdx.x * kPfThreads + threadIdx.x; i < Ip; i += gridDim.x * kPfThreads) {
+        float a = 0.f;
+        if (i < I) {
+            const float g = gu[n * gu_ld + i], u = gu[n * gu_ld + I + i];
+            a = 0.5f * g * (1.0f + erff(g * kInvSqrt2)) * u;
+        }
+        act[n * Ip + i] = __float2bfloat16_rn(a);
+    }
+}
+
+// ---------------------------------------------------------------- launches
+cudaError_t pf_embed(const void *E, int wdtype_bf16, int64_t ld, const int32_t *tok, int N, int H, float scale,
+                     float *x, cudaStream_t s) {
+    if (wdtype_bf16)
+        pf_embed_kernel<__nv_bfloat16><<<N, kPfThreads, 0, s>>>(static_cast<const __nv_bfloat16 *>(E), ld, tok, H,
+                                                                  scale, x);
+    else
+        pf_embed_kernel<float><<<N, kPfThreads, 0, s>>>(static_cast<const float *>(E), ld, tok, H, scale, x);
+    return cudaGetLastError();
+}
+cudaError_t pf_resnorm(const float *base, const float *add, const float *w_add, const float *w_next, float *res,
+                       __nv_bfloat16 *xn, int N, int H, int Kp, float inv_h, cudaStream_t s) {
+    pf_resnorm_kernel<<<N, kPfThreads, 0, s>>>(base, add, w_add, w_next, res, xn, H, Kp, inv_h);
+    return cudaGetLastError();
+}
+cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *q_norm,
+                          const float *k_norm, const float *cos_t, const float *sin_t, const int32_t *row,
+                          const int32_t *pos, float *kc, float *vc, int64_t kv_row_stride, int64_t kv_head_stride,
+                          float inv_hd, cudaStream_t s) {
+    pf_qk_rope_kv_kernel<<<N, kPfThreads, 0, s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, q_norm, k_norm, cos_t, sin_t, row,
+                                                    pos, kc, vc, kv_row_stride, kv_head_stride, inv_hd);
+    return cudaGetLastError();
+}
+cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,
+                         const float *vc, const int32_t *row, const int32_t *pos, int64_t kv_row_stride,
+                         int64_t kv_head_stride, int window, int is_global, float scale, __nv_bfloat16 *out,
+                         int out_ld, cudaStream_t s) {
+    const int64_t tasks = static_cast<int64_t>(N) * Hq;
+    const int blocks = static_cast<int>((tasks + kPfThreads / 32 - 1) / (kPfThreads / 32));
+    pf_attention_kernel<<<blocks, kPfThreads, 0, s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, kc, vc, row, pos, kv_row_stride,
+                                                      kv_head_stride, window, is_global, scale, out, out_ld, N);
+    return cudaGetLastError();
+}
+cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, cudaStream_t s) {
+    const dim3 grid((Ip + kPfThreads - 1) / kPfThreads, N);
+    pf_geglu_kernel<<<grid, kPfThreads, 0, s>>>(gu, I, gu_ld, act, Ip);
+    return cudaGetLastError();
+}
+
+}  // namespace mg

@@ -1,0 +1,66 @@
+"""Batched prefill (prefill_path 1: tcgen05 GEMMs on bf16-rounded inputs) against the oracle.
+
+The oracle feeds the prompt one token at a time in fp32 (the reference's
+prefill loop).  The batched path rounds the projection inputs and weights to
+bf16, so its tolerance is a bf16 one:
+  next-step logits:  max |dev - ref| <= PF_TOL * max |ref|
+  KV cache rows:     max |dev - ref| <= PF_TOL * max |ref| per layer
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from mogemma_b200 import _core, synth
+
+pytestmark = pytest.mark.gpu
+
+PF_TOL = 2e-2
+
+
+def _check(dims: synth.Gemma3Dims, prompt_len: int, *, mode: int = 0, seed: int = 3) -> dict:
+    w = synth.make_weights(dims, seed=seed)
+    kw = dict(capacity=prompt_len + 8, mode="gemma3" if mode else "ref", sliding_window=dims.window)
+    llm = _core.init_model(synth.metadata_of(w), prefill_path=1, **kw)
+    ref = oracle.RefModel(w, max_seq_len=prompt_len + 8, mode=mode, sliding_window=dims.window)
+    toks = [int(t) for t in synth.prompt_ids(prompt_len + 1, dims.vocab, seed=seed + 1)]
+    _core.prefill(llm, toks[:-1])
+    for t in toks[:-1]:
+        ref.step_no_logits(t)
+    kv_err = 0.0
+    for layer in range(dims.layers):
+        for p in (0, prompt_len // 2, prompt_len - 1):
+            k, v = _core.read_kv(llm, layer, p)
+            rk, rv = ref.kv_row(layer, p)
+            kv_err = max(kv_err, float(np.max(np.abs(k - rk))) / float(np.max(np.abs(rk)) + 1e-30),
+                         float(np.max(np.abs(v - rv))) / float(np.max(np.abs(rv)) + 1e-30))
+    dev = _core.step(llm, toks[-1], 0.0, 0, 1.0)
+    r = ref.step(toks[-1])
+    return {"logit_err": float(np.max(np.abs(dev - r))) / float(np.max(np.abs(r))), "kv_err": kv_err}
+
+
+@pytest.mark.parametrize(("prompt_len", "mode"), [(37, 0), (130, 0), (70, 1)])
+def test_batched_prefill_matches_oracle(prompt_len: int, mode: int) -> None:
+    res = _check(synth.tiny(window=32), prompt_len, mode=mode)
+    print(res)
+    assert res["kv_err"] <= PF_TOL and res["logit_err"] <= PF_TOL, res
+
+
+def test_batched_prefill_rows() -> None:
+    d = synth.tiny()
+    w = synth.make_weights(d, seed=9)
+    lens = [23, 9, 40]
+    prompts = [[int(t) for t in synth.prompt_ids(n, d.vocab, seed=20 + i)] for i, n in enumerate(lens)]
+    llm = _core.init_model(synth.metadata_of(w), prefill_path=1, max_batch=3, capacity=64)
+    _core.prefill_rows(llm, prompts)
+    assert llm["_handle"].get_pos()[:3] == lens
+    for b, pr in enumerate(prompts):
+        ref = oracle.RefModel(w, max_seq_len=64)
+        for t in pr:
+            ref.step_no_logits(t)
+        for layer in range(d.layers):
+            k, _ = _core.read_kv(llm, layer, len(pr) - 1, row=b)
+            rk, _ = ref.kv_row(layer, len(pr) - 1)
+            assert float(np.max(np.abs(k - rk))) <= PF_TOL * float(np.max(np.abs(rk)))
