@@ -46,8 +46,9 @@ def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -131,6 +132,59 @@ def cpu_baseline(weights: dict, threads: int, n_tokens: int) -> dict:
     return {"value": (n_tokens - 1) / dt, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{n_tokens - 1} Gemma3-1B decode steps (fp32, full 262144-vocab lm_head) from an empty cache "
                       f"on {threads} host thread(s); attention is <2% of bytes per token at pos<=768"}
+
+
+def run_prefill(args, world: int, rank: int, local: int) -> None:
+    """Prompt tokens/s of the batched prefill (tcgen05 GEMMs), with the
+    token-at-a-time path (the reference's arithmetic) timed beside it."""
+    import torch  # noqa: PLC0415
+
+    from mogemma_b200 import _core, synth  # noqa: PLC0415
+
+    d = synth.CONFIGS[CONFIG]
+    weights = synth.make_weights(d, seed=0, bf16=args.weight_dtype == "bf16")
+    meta = synth.metadata_of(weights)
+    prompt = [int(t) for t in synth.prompt_ids(PROMPT, d.vocab, seed=1)]
+
+    def timed(llm, reps: int) -> float:
+        h = llm["_handle"]
+        stream = torch.cuda.ExternalStream(h.stream, device=torch.device("cuda", local))
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(reps):
+            h.set_pos(0)
+            llm["pos"] = 0
+            _core.prefill(llm, prompt)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) / reps
+
+    llm = _core.init_model(meta, device=local, capacity=PROMPT + 8, weight_dtype=args.weight_dtype, prefill_path=1)
+    for _ in range(args.warmup):
+        timed(llm, 1)
+    ms = timed(llm, args.steps)
+    info = llm["_handle"].info
+    llm["_handle"].close()
+    base = _core.init_model(meta, device=local, capacity=PROMPT + 8, weight_dtype=args.weight_dtype, prefill_path=0)
+    ms_tok = timed(base, 1)
+    base["_handle"].close()
+    params = info.weight_bytes_per_step / (2 if args.weight_dtype == "bf16" else 4) - d.vocab * d.hidden
+    flops = 2.0 * params * PROMPT  # projections; attention adds 4 L Hq hd sum(ctx), small at this length
+    pk = peaks()
+    tf = flops / (ms / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"prefill tokens/s ({CONFIG}, {PROMPT}-token prompt)", "value": PROMPT / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (tcgen05, fp32 accumulate)",
+            "data": "synthetic (seeded N(0,0.02) random-init weights, uniform random prompt ids)",
+            "config": {"workload": f"{CONFIG} batched prefill of {PROMPT} tokens, batch 1, "
+                                   f"{args.weight_dtype} weights (bf16 copies for the tensor cores)"},
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": pk.get("bf16_tflops", 1590.0), "unit": "TFLOP/s",
+                         "frac": tf / pk.get("bf16_tflops", 1590.0), "flops_per_step": flops},
+            "token_at_a_time_ms": ms_tok,
+        }), flush=True)
 
 
 def dist_setup():
@@ -221,6 +275,8 @@ def main() -> None:
     ap.add_argument("--model", default=CONFIG, help="synthetic config (gemma3-270m for small profiling runs)")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled before the timed decode")
     ap.add_argument("--decode", type=int, default=DECODE, help="tokens decoded per step")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="prefill: time the batched tensor-core prefill of --prompt tokens instead of the decode")
     ap.add_argument("--parallel", default="replicas", choices=["replicas", "tp"],
                     help="N>1: independent replicas (weak scaling) or one tensor-parallel model over the N GPUs")
     args = ap.parse_args()
@@ -228,6 +284,9 @@ def main() -> None:
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.workload == "prefill":
+        run_prefill(args, world, rank, local)
         return
 
     import ctypes  # noqa: PLC0415
