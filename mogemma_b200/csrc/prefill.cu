@@ -119,60 +119,128 @@ __global__ void __launch_bounds__(kPfThreads) pf_qk_rope_kv_kernel(
     }
 }
 
-// Causal attention of one (token, q head) per warp over the cached positions
-// lo..pos (layers.mojo:63-94): online softmax, lanes over head dims.  The
-// cache already holds every prompt key of this layer.
+// Causal attention over the cached positions lo..pos (layers.mojo:63-94).  One
+// CTA per (token, kv head) for its GQ q heads (each K/V row read once for the
+// group); its 8 warps take interleaved blocks of 32 keys, one key per lane:
+// a lane forms its key's GQ scores over the whole head (q in shared memory,
+// read as a broadcast), a warp-wide max/sum per head updates that warp's
+// online softmax, and P.V runs with lanes over head dims.  The warps' partial
+// (m, l, acc) are combined in shared memory.
+template <int GQ>
 __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
     const float *qkv, int qkv_ld, int Hq, int Hkv, int hd, int hdp, const float *kc, const float *vc,
     const int32_t *row, const int32_t *pos, int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global,
     float scale, __nv_bfloat16 *out, int out_ld, int N) {
+    constexpr int kQ = GQ > 0 ? GQ : kMaxQPerKv;
     constexpr int kDL = kMaxHeadDim / 32;
-    const int lane = threadIdx.x & 31;
-    const int64_t task = static_cast<int64_t>(blockIdx.x) * (kPfThreads / 32) + (threadIdx.x >> 5);
-    if (task >= static_cast<int64_t>(N) * Hq) return;
-    const int64_t n = task / Hq;
-    const int h = static_cast<int>(task - n * Hq);
-    const int kvh = h / (Hq / Hkv);
+    constexpr int kW = kPfThreads / 32;
+    extern __shared__ __align__(16) float sm_dyn[];  // q [gq][hd] | acc [kW][gq][hd] | m, l [kW][gq]
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int gq = GQ > 0 ? GQ : Hq / Hkv;
+    const int64_t n = blockIdx.x / Hkv;
+    const int kvh = static_cast<int>(blockIdx.x - n * Hkv);
+    float *qs = sm_dyn;
+    float *pacc = qs + gq * hd;
+    float *pm = pacc + kW * gq * hd;
+    float *pl = pm + kW * gq;
     const int p = pos[n];
     const int lo = (!is_global && window > 0 && p - window + 1 > 0) ? p - window + 1 : 0;
-    const float *q = qkv + n * qkv_ld + static_cast<int64_t>(h) * hd;
-    float qr[kDL], acc[kDL];
-#pragma unroll
-    for (int i = 0; i < kDL; ++i) {
-        const int d = lane + 32 * i;
-        qr[i] = d < hd ? q[d] : 0.f;
-        acc[i] = 0.f;
-    }
+    const float *q = qkv + n * qkv_ld + static_cast<int64_t>(kvh) * gq * hd;
+    for (int i = threadIdx.x; i < gq * hd; i += kPfThreads) qs[i] = q[i];
+    __syncthreads();
     const float *kb = kc + row[n] * kv_row_stride + kvh * kv_head_stride;
     const float *vb = vc + row[n] * kv_row_stride + kvh * kv_head_stride;
-    float m = -INFINITY, l = 0.f;
-    for (int t = lo; t <= p; ++t) {
-        const float *k = kb + static_cast<int64_t>(t) * hdp;
-        float s = 0.f;
+    float m[kQ], l[kQ], acc[kQ][kDL];
 #pragma unroll
-        for (int i = 0; i < kDL; ++i) {
-            const int d = lane + 32 * i;
-            if (d < hd) s += qr[i] * k[d];
-        }
-        s = warp_sum(s) * scale;
-        const float m_new = fmaxf(m, s);
-        const float alpha = (m == -INFINITY) ? 0.f : expf(m - m_new);
-        const float e = expf(s - m_new);
-        l = l * alpha + e;
-        const float *v = vb + static_cast<int64_t>(t) * hdp;
+    for (int h = 0; h < kQ; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
 #pragma unroll
-        for (int i = 0; i < kDL; ++i) {
-            const int d = lane + 32 * i;
-            if (d < hd) acc[i] = acc[i] * alpha + e * v[d];
-        }
-        m = m_new;
+        for (int i = 0; i < kDL; ++i) acc[h][i] = 0.f;
     }
-    const float inv_l = 1.0f / l;
-    __nv_bfloat16 *o = out + n * out_ld + static_cast<int64_t>(h) * hd;
+    for (int t0 = lo + 32 * w; t0 <= p; t0 += 32 * kW) {
+        const int t = t0 + lane;
+        const bool valid = t <= p;
+        float s[kQ];
 #pragma unroll
-    for (int i = 0; i < kDL; ++i) {
-        const int d = lane + 32 * i;
-        if (d < hd) o[d] = __float2bfloat16_rn(acc[i] * inv_l);
+        for (int h = 0; h < kQ; ++h) s[h] = 0.f;
+        if (valid) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(kb + static_cast<int64_t>(t) * hdp);
+            for (int d4 = 0; d4 < hd / 4; ++d4) {
+                const float4 kv = k4[d4];
+#pragma unroll
+                for (int h = 0; h < kQ; ++h) {
+                    if (h < gq) {
+                        const float4 qv = *reinterpret_cast<const float4 *>(qs + h * hd + 4 * d4);
+                        s[h] += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+                    }
+                }
+            }
+        }
+        float pr[kQ];
+#pragma unroll
+        for (int h = 0; h < kQ; ++h) {
+            if (h < gq) {
+                const float sh = valid ? s[h] * scale : -INFINITY;
+                const float m_new = fmaxf(m[h], warp_max(sh));
+                const float alpha = (m[h] == -INFINITY) ? 0.f : expf(m[h] - m_new);
+                pr[h] = valid ? expf(sh - m_new) : 0.f;
+                l[h] = l[h] * alpha + warp_sum(pr[h]);
+#pragma unroll
+                for (int i = 0; i < kDL; ++i) acc[h][i] *= alpha;
+                m[h] = m_new;
+            }
+        }
+        const int nb = min(32, p - t0 + 1);
+        for (int j = 0; j < nb; ++j) {
+            const float *v = vb + static_cast<int64_t>(t0 + j) * hdp;
+            float vv[kDL];
+#pragma unroll
+            for (int i = 0; i < kDL; ++i) {
+                const int d = lane + 32 * i;
+                vv[i] = d < hd ? v[d] : 0.f;
+            }
+#pragma unroll
+            for (int h = 0; h < kQ; ++h) {
+                if (h < gq) {
+                    const float pj = __shfl_sync(0xffffffffu, pr[h], j);
+#pragma unroll
+                    for (int i = 0; i < kDL; ++i) acc[h][i] += pj * vv[i];
+                }
+            }
+        }
+    }
+    // combine the warps' partials
+#pragma unroll
+    for (int h = 0; h < kQ; ++h) {
+        if (h < gq) {
+            if (lane == 0) {
+                pm[w * gq + h] = m[h];
+                pl[w * gq + h] = l[h];
+            }
+#pragma unroll
+            for (int i = 0; i < kDL; ++i) {
+                const int d = lane + 32 * i;
+                if (d < hd) pacc[(w * gq + h) * hd + d] = acc[h][i];
+            }
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < gq * hd; e += kPfThreads) {
+        const int h = e / hd, d = e - h * hd;
+        float M = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < kW; ++u) M = fmaxf(M, pm[u * gq + h]);
+        float L = 0.f, o = 0.f;
+#pragma unroll
+        for (int u = 0; u < kW; ++u) {
+            const float mu = pm[u * gq + h];
+            if (mu == -INFINITY) continue;  // a warp that saw no key
+            const float f = expf(mu - M);
+            L += pl[u * gq + h] * f;
+            o += pacc[(u * gq + h) * hd + d] * f;
+        }
+        out[n * out_ld + static_cast<int64_t>(kvh * gq + h) * hd + d] = __float2bfloat16_rn(o / L);
     }
 }
 
@@ -217,10 +285,28 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
                          const float *vc, const int32_t *row, const int32_t *pos, int64_t kv_row_stride,
                          int64_t kv_head_stride, int window, int is_global, float scale, __nv_bfloat16 *out,
                          int out_ld, cudaStream_t s) {
-    const int64_t tasks = static_cast<int64_t>(N) * Hq;
-    const int blocks = static_cast<int>((tasks + kPfThreads / 32 - 1) / (kPfThreads / 32));
-    pf_attention_kernel<<<blocks, kPfThreads, 0, s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, kc, vc, row, pos, kv_row_stride,
-                                                      kv_head_stride, window, is_global, scale, out, out_ld, N);
+    const int blocks = N * Hkv;
+    const int gq = Hq / Hkv;
+    const size_t smem = sizeof(float) * (static_cast<size_t>(gq) * hd * (1 + kPfThreads / 32) + 2 * (kPfThreads / 32) * gq);
+#define MG_PF_ATT(G)                                                                                                \
+    do {                                                                                                            \
+        if (smem > 48 * 1024) {                                                                                     \
+            const cudaError_t e = cudaFuncSetAttribute(pf_attention_kernel<G>,                                      \
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
+                                                       static_cast<int>(smem));                                     \
+            if (e != cudaSuccess) return e;                                                                         \
+        }                                                                                                           \
+        pf_attention_kernel<G><<<blocks, kPfThreads, smem, s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, kc, vc, row, pos,   \
+                                                                kv_row_stride, kv_head_stride, window, is_global,   \
+                                                                scale, out, out_ld, N);                             \
+    } while (0)
+    switch (Hq / Hkv) {
+        case 1: MG_PF_ATT(1); break;
+        case 2: MG_PF_ATT(2); break;
+        case 4: MG_PF_ATT(4); break;
+        default: MG_PF_ATT(0); break;
+    }
+#undef MG_PF_ATT
     return cudaGetLastError();
 }
 cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, cudaStream_t s) {
