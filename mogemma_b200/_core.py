@@ -227,8 +227,9 @@ class ModelHandle:
         _check(_lib.mg_tp_connect(self.ptr, ctypes.cast(buf, _P), len(handles)))
 
     def get_pos(self) -> list[int]:
-        out = np.zeros(8, np.int32)
-        _check(_lib.mg_get_pos(self.ptr, out.ctypes.data_as(_I32P), 8))
+        n = max(8, int(self.info.max_batch))
+        out = np.zeros(n, np.int32)
+        _check(_lib.mg_get_pos(self.ptr, out.ctypes.data_as(_I32P), n))
         return [int(x) for x in out]
 
 

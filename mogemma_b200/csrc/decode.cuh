@@ -19,6 +19,7 @@ constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kStageBytes = 36864;   // one ring stage
 constexpr int kMaxRows = 8;          // batch rows per persistent launch
 constexpr int kMaxTp = 8;            // tensor-parallel ranks
+constexpr int kMaxBatch = 64;        // rows a model holds (more than kMaxRows: batched tensor-core steps)
 constexpr int kMaxHeadDim = 256;
 constexpr int kMaxQPerKv = 8;
 constexpr int kMaxTopK = 64;         // fused top-k width

@@ -152,6 +152,11 @@ struct mg_model {
     float *pf_x = nullptr, *pf_r = nullptr, *pf_c = nullptr;
     __nv_bfloat16 *pf_xn = nullptr;
     int32_t *pf_tok = nullptr, *pf_row = nullptr, *pf_pos = nullptr;
+    __nv_bfloat16 *pf_lm = nullptr;  // bf16 lm_head [V][Hp] for batched decode steps
+
+    // rows: Bmax in the KV cache; Bdec the most the persistent decode kernel
+    // stages (shared memory); steps with more rows take the batched path
+    int Bdec = 1, nrows = kMaxRows;
 };
 
 template <typename T>
@@ -300,7 +305,8 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     m->wdtype = opt ? opt->weight_dtype : MG_F32;
     if (m->wdtype != MG_F32 && m->wdtype != MG_BF16) return fail(MG_ERR_INVALID, "weight_dtype must be F32 or BF16");
     m->Bmax = opt && opt->max_batch > 0 ? opt->max_batch : 1;
-    if (m->Bmax > kMaxRows) return fail(MG_ERR_UNSUPPORTED, "max_batch %d exceeds %d", m->Bmax, kMaxRows);
+    if (m->Bmax > kMaxBatch) return fail(MG_ERR_UNSUPPORTED, "max_batch %d exceeds %d", m->Bmax, kMaxBatch);
+    m->nrows = std::max(m->Bmax, kMaxRows);
     m->cap = opt && opt->capacity > 0 ? opt->capacity : 8192;
     m->seed = opt ? opt->seed : 0;
     m->decode_path = opt ? opt->decode_path : 0;
@@ -423,27 +429,40 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     CU(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->dev));
     const int Kmax = std::max(m->Hp, std::max(m->Ap, m->Ip));
     const int Gq = m->Hq / m->Hkv;
-    // shared activation stage: GEMV inputs; o_proj input + split-KV weights;
-    // attention scratch; top-k selection scratch
-    int xs = m->Bmax * Kmax;
-    xs = std::max(xs, m->Bmax * (m->Hp + m->H));  // normed input + staged residual rows
-    xs = std::max(xs, m->Bmax * (m->Ap + m->Hq * kMaxChunks));
-    xs = std::max(xs, (Gq + 2) * hd + Gq * kAttTile + 3 * kMaxQPerKv + 2 * hd + m->Bmax * hd +
-                          kConsumerThreads * Gq + 8);
-    xs = std::max(xs, static_cast<int>((sizeof(uint32_t) * 264 + sizeof(uint64_t) * 1024 + kMaxTopK * 8 * 2 +
-                                        kMaxTopK * 4) / 4 + 16));
-    m->xs_floats = (xs + 31) / 32 * 32;
+    // shared activation stage for Bd rows: GEMV inputs; o_proj input +
+    // split-KV weights; attention scratch; top-k selection scratch.  The
+    // persistent kernel takes the most rows (<= kMaxRows) whose stage leaves at
+    // least two ring stages; steps with more rows take the batched path.
     const size_t static_smem =
         (m->wdtype == MG_F32 ? decode_static_smem<float>() : decode_static_smem<__nv_bfloat16>()) + 64;
+    auto stage_floats = [&](int Bd) {
+        int xs = Bd * Kmax;
+        xs = std::max(xs, Bd * (m->Hp + m->H));  // normed input + staged residual rows
+        xs = std::max(xs, Bd * (m->Ap + m->Hq * kMaxChunks));
+        xs = std::max(xs, (Gq + 2) * hd + Gq * kAttTile + 3 * kMaxQPerKv + 2 * hd + Bd * hd + kConsumerThreads * Gq +
+                              8);
+        xs = std::max(xs, static_cast<int>((sizeof(uint32_t) * 264 + sizeof(uint64_t) * 1024 + kMaxTopK * 8 * 2 +
+                                            kMaxTopK * 4) / 4 + 16));
+        return (xs + 31) / 32 * 32;
+    };
     m->S = 0;
-    for (int S = 8; S >= 2; --S)
-        if (decode_smem_bytes(S, m->xs_floats, L) + static_smem <= static_cast<size_t>(max_smem)) {
-            m->S = S;
-            break;
-        }
+    for (int Bd = std::min(m->Bmax, kMaxRows); Bd >= 1 && m->S == 0; --Bd) {
+        m->xs_floats = stage_floats(Bd);
+        for (int S = 8; S >= 2; --S)
+            if (decode_smem_bytes(S, m->xs_floats, L) + static_smem <= static_cast<size_t>(max_smem)) {
+                m->S = S;
+                m->Bdec = Bd;
+                break;
+            }
+    }
     if (m->S < 2)
         return fail(MG_ERR_UNSUPPORTED, "activation stage of %d floats leaves no room for the weight ring",
                     m->xs_floats);
+    if (m->Bmax > m->Bdec && (m->prefill_path != 1 || m->tp > 1))
+        return fail(MG_ERR_UNSUPPORTED,
+                    "max_batch %d: the persistent decode kernel holds %d rows of this model; more rows need "
+                    "prefill_path 1 (batched tensor-core steps) without tensor parallelism",
+                    m->Bmax, m->Bdec);
     m->smem = decode_smem_bytes(m->S, m->xs_floats, L);
     if (m->wdtype == MG_F32) {
         CU(decode_prepare<float>(m->smem));
@@ -550,6 +569,10 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     TRY(upload_tiled(m, rows_view(*lmh, m->v0), m->V, m->H, 0, m->lm_head, wd, m->Hp, sh_h, 0, staging,
                      staging_bytes));
     m->weight_bytes += static_cast<int64_t>(we) * m->V * m->H;
+    if (m->Bmax > m->Bdec) {  // lm_head for batched decode steps
+        TRY(dalloc(m, &m->pf_lm, static_cast<size_t>(m->V) * m->Hp));
+        TRY(upload_matrix(m, *lmh, m->V, m->H, m->pf_lm, MG_BF16, m->Hp, staging, staging_bytes));
+    }
     // embedding rows are gathered, so they stay row-major (a separate copy even
     // when lm_head is tied to them, convert.py:129-131)
     TRY(dalloc(m, reinterpret_cast<char **>(&m->embed), static_cast<size_t>(m->V_g) * m->H * we));
@@ -619,14 +642,14 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     }
     TRY(dalloc(m, &m->emb_acc, static_cast<size_t>(B) * m->H));
     TRY(dalloc(m, &m->cand_key, static_cast<size_t>(B) * m->G * kMaxTopK));
-    TRY(dalloc(m, &m->tok, kMaxRows));
-    TRY(dalloc(m, &m->pos, kMaxRows));
-    TRY(dalloc(m, &m->uniforms, kMaxRows));
+    TRY(dalloc(m, &m->tok, m->nrows));
+    TRY(dalloc(m, &m->pos, m->nrows));
+    TRY(dalloc(m, &m->uniforms, m->nrows));
     m->sync_words = num_phases(L) + 1;
     TRY(dalloc(m, &m->sync, m->sync_words));
     TRY(dalloc(m, &m->err, 1));
     CU(cudaMallocHost(&m->pinned, 4096));
-    m->h_pos.assign(kMaxRows, 0);
+    m->h_pos.assign(m->nrows, 0);
     CU(cudaStreamSynchronize(m->stream));
     cudaFree(staging);
     m->allocs.erase(std::find(m->allocs.begin(), m->allocs.end(), staging));
@@ -884,13 +907,16 @@ static mg_status step_impl(mg_model *m, int batch, float *logits_host, int32_t *
         mg_status st = check_device(m);
         if (st != MG_OK) {
             for (int b = 0; b < batch; ++b) m->h_pos[b] -= 1;
-            CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+            CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice));
             return st;
         }
         if (sampled_host && s) memcpy(sampled_host, m->pinned, sizeof(int32_t) * batch);
     }
     return MG_OK;
 }
+
+static mg_status step_batched(mg_model *m, int batch, const int32_t *tok_host, const mg_sampling *s,
+                              int32_t *out_tokens_dev);
 
 extern "C" mg_status mg_step(mg_model *m, const int32_t *token_ids_host, int32_t batch, float *logits_host,
                              int32_t *sampled_host, const mg_sampling *s) {
@@ -902,7 +928,24 @@ extern "C" mg_status mg_step(mg_model *m, const int32_t *token_ids_host, int32_t
             return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", token_ids_host[b], m->V_g);
     memcpy(m->pinned, token_ids_host, sizeof(int32_t) * batch);
     CU(cudaMemcpyAsync(m->tok, m->pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, m->stream));
-    return step_impl(m, batch, logits_host, sampled_host, s, true);
+    if (batch <= m->Bdec) return step_impl(m, batch, logits_host, sampled_host, s, true);
+    // more rows than the persistent kernel holds: batched tensor-core step
+    for (int b = 0; b < batch; ++b)
+        if (m->h_pos[b] >= m->cap) return fail(MG_ERR_SEQ_EXCEEDED, "Sequence length exceeded");
+    const std::vector<int32_t> pos0 = m->h_pos;
+    mg_status st = step_batched(m, batch, nullptr, s, nullptr);
+    if (st == MG_OK && logits_host)
+        CU(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * batch * m->V, cudaMemcpyDeviceToHost, m->stream));
+    if (st == MG_OK && sampled_host && s)
+        CU(cudaMemcpyAsync(m->pinned, m->tok, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, m->stream));
+    if (st == MG_OK) st = check_device(m);
+    if (st != MG_OK) {
+        m->h_pos = pos0;
+        CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice));
+        return st;
+    }
+    if (sampled_host && s) memcpy(sampled_host, m->pinned, sizeof(int32_t) * batch);
+    return MG_OK;
 }
 
 extern "C" mg_status mg_set_tokens(mg_model *m, const int32_t *token_ids_host, int32_t batch) {
@@ -934,7 +977,9 @@ extern "C" mg_status mg_generate(mg_model *m, int32_t n_steps, int32_t batch, co
     }
     const SampleCfg sc = sample_cfg(m, s);
     const std::vector<int32_t> pos0 = m->h_pos;
-    for (int t = 0; t < n_steps; ++t) {
+    for (int t = 0; t < n_steps && batch > m->Bdec; ++t)  // batched tensor-core steps
+        TRY(step_batched(m, batch, nullptr, s, m->out_tokens + static_cast<int64_t>(t) * batch));
+    for (int t = 0; t < n_steps && batch <= m->Bdec; ++t) {
         DecodeParams p = base_params(m, batch);
         p.lm_mode = kLmLogits;
         p.topk = sc.fused ? sc.topk : 0;
@@ -964,7 +1009,7 @@ extern "C" mg_status mg_generate(mg_model *m, int32_t n_steps, int32_t batch, co
     mg_status st = check_device(m);
     if (st != MG_OK) {
         m->h_pos = pos0;
-        CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice));
     }
     return st;
 }
@@ -977,7 +1022,7 @@ static mg_status upload_ids(mg_model *m, const int32_t *ids, const int32_t *lens
         m->ids = buf;
         m->ids_cap = need;
     }
-    if (!m->nvalid) TRY(dalloc(m, &m->nvalid, kMaxRows));
+    if (!m->nvalid) TRY(dalloc(m, &m->nvalid, m->nrows));
     for (int b = 0; b < batch; ++b) {
         if (lens[b] < 0 || lens[b] > max_len) return fail(MG_ERR_INVALID, "row %d length %d outside [0, %d]", b, lens[b], max_len);
         for (int t = 0; t < lens[b]; ++t) {
@@ -992,16 +1037,8 @@ static mg_status upload_ids(mg_model *m, const int32_t *ids, const int32_t *lens
 
 // Batched prefill (prefill_path 1): all prompt tokens of all rows per layer,
 // projections on the tensor cores (prefill.cu, gemm_tc.cu).
-static mg_status prefill_batched(mg_model *m, const int32_t *ids, const int32_t *lens, int batch, int max_len) {
-    std::vector<int32_t> tok, row, pos;
-    for (int b = 0; b < batch; ++b)
-        for (int t = 0; t < lens[b]; ++t) {
-            tok.push_back(ids[static_cast<int64_t>(b) * max_len + t]);
-            row.push_back(b);
-            pos.push_back(m->h_pos[b] + t);
-        }
-    const int N = static_cast<int>(tok.size());
-    if (N == 0) return MG_OK;
+// Workspace for N packed tokens (kept for later calls).
+static mg_status pf_reserve(mg_model *m, int N) {
     if (N > m->pf_cap) {  // workspace for N packed tokens (kept for later calls)
         const int cap = std::max(N, 256);
         m->pf_kx = std::max(m->Hp, std::max(m->Ap, m->Ip));
@@ -1015,10 +1052,13 @@ static mg_status prefill_batched(mg_model *m, const int32_t *ids, const int32_t 
         TRY(dalloc(m, &m->pf_pos, cap));
         m->pf_cap = cap;
     }
+    return MG_OK;
+}
+
+// Every layer for the N tokens in pf_tok / pf_row / pf_pos: K/V into the
+// cache, and pf_xn = bf16(final-norm of the last layer's output) per token.
+static mg_status pf_layers(mg_model *m, int N) {
     cudaStream_t st = m->stream;
-    CU(cudaMemcpyAsync(m->pf_tok, tok.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
-    CU(cudaMemcpyAsync(m->pf_row, row.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
-    CU(cudaMemcpyAsync(m->pf_pos, pos.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
     const float inv_h = 1.0f / static_cast<float>(m->H), inv_hd = 1.0f / static_cast<float>(m->hd);
     const float att_scale = 1.0f / sqrtf(static_cast<float>(m->hd));
     CU(pf_embed(m->embed, m->wdtype == MG_BF16, m->embed_ld, m->pf_tok, N, m->H, sqrtf(static_cast<float>(m->H)),
@@ -1052,6 +1092,61 @@ static mg_status prefill_batched(mg_model *m, const int32_t *ids, const int32_t 
     return MG_OK;
 }
 
+static mg_status prefill_batched(mg_model *m, const int32_t *ids, const int32_t *lens, int batch, int max_len) {
+    std::vector<int32_t> tok, row, pos;
+    for (int b = 0; b < batch; ++b)
+        for (int t = 0; t < lens[b]; ++t) {
+            tok.push_back(ids[static_cast<int64_t>(b) * max_len + t]);
+            row.push_back(b);
+            pos.push_back(m->h_pos[b] + t);
+        }
+    const int N = static_cast<int>(tok.size());
+    if (N == 0) return MG_OK;
+    TRY(pf_reserve(m, N));
+    cudaStream_t st = m->stream;
+    CU(cudaMemcpyAsync(m->pf_tok, tok.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+    CU(cudaMemcpyAsync(m->pf_row, row.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+    CU(cudaMemcpyAsync(m->pf_pos, pos.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+    return pf_layers(m, N);
+}
+
+// One decode step for rows [0, batch) on the batched path (more rows than the
+// persistent kernel holds): the layers for one token per row, the lm_head as a
+// tcgen05 GEMM into logits [batch][V], then the token draw of
+// _sample_next_token (model.py:103-150) over each row with the general sampler.
+// tok_host null: the rows' current tokens on the device (m->tok).
+static mg_status step_batched(mg_model *m, int batch, const int32_t *tok_host, const mg_sampling *s,
+                              int32_t *out_tokens_dev) {
+    TRY(pf_reserve(m, batch));
+    cudaStream_t st = m->stream;
+    std::vector<int32_t> row(batch), pos(batch);
+    for (int b = 0; b < batch; ++b) {
+        row[b] = b;
+        pos[b] = m->h_pos[b];
+    }
+    if (tok_host)
+        CU(cudaMemcpyAsync(m->pf_tok, tok_host, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
+    else
+        CU(cudaMemcpyAsync(m->pf_tok, m->tok, sizeof(int32_t) * batch, cudaMemcpyDeviceToDevice, st));
+    CU(cudaMemcpyAsync(m->pf_row, row.data(), sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
+    CU(cudaMemcpyAsync(m->pf_pos, pos.data(), sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
+    TRY(pf_layers(m, batch));
+    CU(gemm_bf16_tc(m->pf_xn, m->Hp, m->pf_lm, m->Hp, m->logits, m->V, batch, m->V, m->Hp, m->err, st));
+    if (s) {
+        const double *u = nullptr;
+        if (s->uniforms_host) {
+            CU(cudaMemcpyAsync(m->uniforms, s->uniforms_host, sizeof(double) * batch, cudaMemcpyHostToDevice, st));
+            u = m->uniforms;
+        }
+        CU(sample_rows_launch(m->logits, m->V, batch, m->V, s->temperature, s->top_k, s->top_p, u, m->seed,
+                              m->rng_offset, out_tokens_dev, m->tok, st));
+        m->rng_offset += 1;
+    }
+    for (int b = 0; b < batch; ++b) m->h_pos[b] += 1;
+    CU(cudaMemcpyAsync(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice, st));
+    return MG_OK;
+}
+
 extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
                                 int32_t max_len) {
     if (!m || !token_ids_host || !lens_host) return fail(MG_ERR_INVALID, "null argument");
@@ -1069,16 +1164,19 @@ extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, cons
         mg_status st = prefill_batched(m, token_ids_host, lens_host, batch, max_len);
         if (st == MG_OK) {
             for (int b = 0; b < batch; ++b) m->h_pos[b] = pos0[b] + lens_host[b];
-            CU(cudaMemcpyAsync(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice,
+            CU(cudaMemcpyAsync(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice,
                                m->stream));
             st = check_device(m);
         }
         if (st != MG_OK) {
             m->h_pos = pos0;
-            CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+            CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice));
         }
         return st;
     }
+    if (batch > m->Bdec)
+        return fail(MG_ERR_UNSUPPORTED, "prefill of %d rows needs prefill_path 1 (the decode kernel holds %d)", batch,
+                    m->Bdec);
     for (int t = 0; t < longest; ++t) {
         DecodeParams p = base_params(m, batch);
         p.lm_mode = kLmNone;
@@ -1095,7 +1193,7 @@ extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, cons
     mg_status st = check_device(m);
     if (st != MG_OK) {
         m->h_pos = pos0;
-        CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice));
     }
     return st;
 }
@@ -1111,12 +1209,12 @@ extern "C" mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const 
     }
     const std::vector<int32_t> pos_saved = m->h_pos;
     std::vector<float> acc(static_cast<size_t>(m->Bmax) * m->H);
-    for (int b0 = 0; b0 < batch; b0 += m->Bmax) {
-        const int nb = std::min(m->Bmax, batch - b0);
+    for (int b0 = 0; b0 < batch; b0 += m->Bdec) {
+        const int nb = std::min(m->Bdec, batch - b0);
         int longest = 0;
         for (int b = 0; b < nb; ++b) longest = std::max(longest, lens_host[b0 + b]);
         TRY(upload_ids(m, token_ids_host + static_cast<int64_t>(b0) * max_len, lens_host + b0, nb, max_len));
-        CU(cudaMemsetAsync(m->pos, 0, sizeof(int32_t) * kMaxRows, m->stream));
+        CU(cudaMemsetAsync(m->pos, 0, sizeof(int32_t) * m->nrows, m->stream));
         CU(cudaMemsetAsync(m->emb_acc, 0, sizeof(float) * m->Bmax * m->H, m->stream));
         for (int t = 0; t < longest; ++t) {
             DecodeParams p = base_params(m, nb);
@@ -1136,7 +1234,7 @@ extern "C" mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const 
         }
     }
     m->h_pos = pos_saved;
-    CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice));
     return MG_OK;
 }
 
@@ -1145,16 +1243,16 @@ extern "C" mg_status mg_set_pos(mg_model *m, int32_t row, int32_t pos) {
     if (row >= m->Bmax || row < -1) return fail(MG_ERR_INVALID, "row %d outside [-1, %d)", row, m->Bmax);
     if (pos < 0 || pos > m->cap) return fail(MG_ERR_INVALID, "pos %d outside [0, %d]", pos, m->cap);
     CU(cudaSetDevice(m->dev));
-    for (int b = 0; b < kMaxRows; ++b)
+    for (int b = 0; b < m->nrows; ++b)
         if (row == -1 || row == b) m->h_pos[b] = pos;
-    CU(cudaMemcpyAsync(m->pos, m->h_pos.data(), sizeof(int32_t) * kMaxRows, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice, m->stream));
     CU(cudaStreamSynchronize(m->stream));
     return MG_OK;
 }
 
 extern "C" mg_status mg_get_pos(const mg_model *m, int32_t *pos_host, int32_t n) {
     if (!m || !pos_host) return fail(MG_ERR_INVALID, "null argument");
-    for (int i = 0; i < n && i < kMaxRows; ++i) pos_host[i] = m->h_pos[i];
+    for (int i = 0; i < n && i < m->nrows; ++i) pos_host[i] = m->h_pos[i];
     return MG_OK;
 }
 

@@ -64,3 +64,31 @@ def test_batched_prefill_rows() -> None:
             k, _ = _core.read_kv(llm, layer, len(pr) - 1, row=b)
             rk, _ = ref.kv_row(layer, len(pr) - 1)
             assert float(np.max(np.abs(k - rk))) <= PF_TOL * float(np.max(np.abs(rk)))
+
+
+def test_batched_decode_rows_beyond_persistent_kernel() -> None:
+    """16 rows (the persistent kernel holds 8): tensor-core decode steps, each
+    row against its own oracle run."""
+    d = synth.tiny()
+    w = synth.make_weights(d, seed=13)
+    rows = 16
+    prompts = [[int(t) for t in synth.prompt_ids(5 + 3 * i, d.vocab, seed=40 + i)] for i in range(rows)]
+    llm = _core.init_model(synth.metadata_of(w), prefill_path=1, max_batch=rows, capacity=96)
+    _core.prefill_rows(llm, [p[:-1] for p in prompts])
+    logits, drawn = _core.step_rows(llm, [p[-1] for p in prompts], sampling=(0.0, 0, 1.0))
+    assert logits.shape == (rows, d.vocab)
+    for b, pr in enumerate(prompts):
+        ref = oracle.RefModel(w, max_seq_len=96)
+        for t in pr[:-1]:
+            ref.step_no_logits(t)
+        r = ref.step(pr[-1])
+        assert float(np.max(np.abs(logits[b] - r))) <= PF_TOL * float(np.max(np.abs(r))), b
+        assert int(drawn[b]) == int(np.argmax(logits[b]))  # greedy draw over the step's own logits
+    # a device-side loop over the 16 rows keeps each row's position
+    h = llm["_handle"]
+    before = h.get_pos()[:rows]
+    out = np.zeros((4, rows), np.int32)
+    s, _keep = _core._sampling(0.7, 20, 1.0)
+    _core._check(_core.lib().mg_generate(h.ptr, 4, rows, _core.ctypes.byref(s), out.ctypes.data_as(_core._I32P)))
+    assert h.get_pos()[:rows] == [p + 4 for p in before]
+    assert ((out >= 0) & (out < d.vocab)).all()
