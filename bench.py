@@ -94,8 +94,11 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def algorithmic_bytes(info, pos0: int, n: int) -> float:
-    """Average bytes one decode-kernel launch (of one rank) must move for positions pos0..pos0+n-1."""
+def algorithmic_bytes(info, pos0: int, n: int, rows: int = 1) -> float:
+    """Average bytes one decode step (of one rank) must move for positions pos0..pos0+n-1 of `rows` rows.
+
+    Beyond 8 rows the step runs on the batched path, which streams bf16 copies of the weights and writes and
+    reads back [rows, vocab] logits."""
     tp = max(1, int(info.tp_size))
     kv_heads = info.num_kv_heads // tp if info.num_kv_heads % tp == 0 else 1  # this rank's kv heads
     kv_row = 2 * kv_heads * info.head_dim * 4  # K+V fp32, one layer, one position
@@ -104,7 +107,11 @@ def algorithmic_bytes(info, pos0: int, n: int) -> float:
     kv_write = info.num_layers * kv_row
     logits = info.vocab_size // tp * 4
     emb_row = info.hidden_size * (4 if info.weight_dtype == 0 else 2)
-    return float(info.weight_bytes_per_step + kv_read + kv_write + logits + emb_row)
+    weights = float(info.weight_bytes_per_step)
+    if rows > 8:
+        weights = weights / (4 if info.weight_dtype == 0 else 2) * 2
+        logits *= 2
+    return weights + rows * (kv_read + kv_write + logits + emb_row)
 
 
 # DRAM bytes (read + write) per decode launch over its algorithmic bytes, from
@@ -275,6 +282,8 @@ def main() -> None:
     ap.add_argument("--model", default=CONFIG, help="synthetic config (gemma3-270m for small profiling runs)")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled before the timed decode")
     ap.add_argument("--decode", type=int, default=DECODE, help="tokens decoded per step")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="decode rows (beyond the persistent kernel's rows: batched tensor-core steps)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
                     help="prefill: time the batched tensor-core prefill of --prompt tokens instead of the decode")
     ap.add_argument("--parallel", default="replicas", choices=["replicas", "tp"],
@@ -298,26 +307,31 @@ def main() -> None:
     d = synth.CONFIGS[CONFIG]
     weights = synth.make_weights(d, seed=0, bf16=args.weight_dtype == "bf16")
     tp = args.parallel == "tp" and world > 1
+    B = args.batch
+    opts = dict(device=local, capacity=PROMPT + DECODE, max_batch=B, weight_dtype=args.weight_dtype,
+                prefill_path=1 if B > 1 else 0)
     if tp:  # every rank holds its shard; the same seed on every rank draws the same tokens
-        llm = _core.init_model_tp(synth.metadata_of(weights), device=local, capacity=PROMPT + DECODE, max_batch=1,
-                                  weight_dtype=args.weight_dtype, seed=1234)
+        llm = _core.init_model_tp(synth.metadata_of(weights), seed=1234, **opts)
     else:
-        llm = _core.init_model(synth.metadata_of(weights), device=local, capacity=PROMPT + DECODE, max_batch=1,
-                               weight_dtype=args.weight_dtype, seed=1234 + rank)
+        llm = _core.init_model(synth.metadata_of(weights), seed=1234 + rank, **opts)
     h = llm["_handle"]
     info = h.info
     lib = _core.lib()
-    prompt = [int(t) for t in synth.prompt_ids(PROMPT, d.vocab, seed=1)]
-    _core.prefill(llm, prompt[:-1])
+    prompts = [[int(t) for t in synth.prompt_ids(PROMPT, d.vocab, seed=1 + b)] for b in range(B)]
+    prompt = prompts[0]
+    if B == 1:
+        _core.prefill(llm, prompt[:-1])
+    else:
+        _core.prefill_rows(llm, [p[:-1] for p in prompts])
     s, _keep = _core._sampling(TEMPERATURE, TOP_K, TOP_P)
-    first = np.array([prompt[-1]], np.int32)
+    first = np.array([p[-1] for p in prompts], np.int32)
     stream = torch.cuda.ExternalStream(h.stream, device=torch.device("cuda", local))
 
     def device_step() -> None:
-        # positions 511.. : feed the last prompt token, then 255 sampled tokens
-        _core._check(lib.mg_set_pos(h.ptr, 0, PROMPT - 1))
-        _core._check(lib.mg_set_tokens(h.ptr, first.ctypes.data_as(_core._I32P), 1))
-        _core._check(lib.mg_generate(h.ptr, DECODE, 1, ctypes.byref(s), None))
+        # positions 511.. : feed the last prompt token, then 255 sampled tokens (every row)
+        _core._check(lib.mg_set_pos(h.ptr, -1, PROMPT - 1))
+        _core._check(lib.mg_set_tokens(h.ptr, first.ctypes.data_as(_core._I32P), B))
+        _core._check(lib.mg_generate(h.ptr, DECODE, B, ctypes.byref(s), None))
 
     for _ in range(args.warmup):
         device_step()
@@ -336,24 +350,24 @@ def main() -> None:
     ms = ev0.elapsed_time(ev1)
     ms = dist_max(ms, world)
     streams = 1 if tp else world
-    tokens = args.steps * DECODE * streams
+    tokens = args.steps * DECODE * streams * B
     value = tokens / (ms / 1000.0)
     ms_launch = ms / (args.steps * DECODE)
-    bytes_launch = algorithmic_bytes(info, PROMPT - 1, DECODE)
+    bytes_launch = algorithmic_bytes(info, PROMPT - 1, DECODE, B)
     achieved = bytes_launch / (ms_launch / 1000.0) / 1e9
     pk = peaks()
 
     # e2e: per-token C-ABI call with host buffers (token id in, sampled id out)
-    ids = np.zeros(1, np.int32)
-    out = np.zeros(1, np.int32)
+    ids = np.zeros(B, np.int32)
+    out = np.zeros(B, np.int32)
     idp, outp = ids.ctypes.data_as(_core._I32P), out.ctypes.data_as(_core._I32P)
 
     def e2e_step() -> None:
-        _core._check(lib.mg_set_pos(h.ptr, 0, PROMPT - 1))
-        ids[0] = prompt[-1]
+        _core._check(lib.mg_set_pos(h.ptr, -1, PROMPT - 1))
+        ids[:] = first
         for _ in range(DECODE):
-            _core._check(lib.mg_step(h.ptr, idp, 1, None, outp, ctypes.byref(s)))
-            ids[0] = out[0]
+            _core._check(lib.mg_step(h.ptr, idp, B, None, outp, ctypes.byref(s)))
+            ids[:] = out
 
     e2e_step()
     barrier(world)
@@ -362,7 +376,7 @@ def main() -> None:
     for _ in range(e2e_steps):
         e2e_step()
     e2e_s = dist_max(time.perf_counter() - t0, world)
-    e2e_value = e2e_steps * DECODE * streams / e2e_s
+    e2e_value = e2e_steps * DECODE * streams * B / e2e_s
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -374,9 +388,9 @@ def main() -> None:
             "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": args.weight_dtype,
             "data": "synthetic (seeded N(0,0.02) random-init weights, uniform random prompt ids)",
-            "config": {"workload": f"{CONFIG} batch-1 decode: {PROMPT}-token prompt then {DECODE} tokens "
+            "config": {"workload": f"{CONFIG} batch-{B} decode: {PROMPT}-token prompt then {DECODE} tokens "
                                    f"(T={TEMPERATURE}, top-k {TOP_K}), {args.weight_dtype} weights",
-                       "model": CONFIG, "global_batch": streams, "seq_len": PROMPT + DECODE,
+                       "model": CONFIG, "global_batch": streams * B, "seq_len": PROMPT + DECODE,
                        "parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1 else "single GPU",
                        "l2": f"inputs larger than L2 ({info.weight_bytes_per_step / 1e9:.2f} GB of weights per token)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * DECODE,
@@ -386,11 +400,12 @@ def main() -> None:
                          "traffic": (bytes_launch * TRAFFIC_RATIO[(CONFIG, args.weight_dtype)]
                                      if (CONFIG, args.weight_dtype) in TRAFFIC_RATIO else None),
                          "traffic_source": "ncu dram__bytes_read+write of a Gemma3-270M launch, scaled by bytes",
-                         "peak_source": pk["source"], "kernel": "decode_kernel (one launch per token)",
+                         "peak_source": pk["source"], "kernel": ("decode_kernel (one launch per token)" if B <= 8 else
+                                    "batched step: tcgen05 GEMMs + prefill kernels per layer, lm_head GEMM, sampler"),
                          "algorithmic_bytes_per_launch": bytes_launch},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
-            "gpu_launches": args.steps * DECODE,
+            "gpu_launches": args.steps * DECODE * (1 if B <= 8 else 9 * d.layers + 4),
             "ms_per_token": ms_launch,
         }
         print(json.dumps(line), flush=True)
