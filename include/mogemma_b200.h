@@ -178,6 +178,19 @@ mg_status mg_sample_static(const float *logits_dev, int64_t ld, int32_t batch, i
 mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
                    int32_t max_len, float *out_host);
 
+/* ---- bidirectional encoder embeddings (no counterpart in the reference, whose
+ * generate_embeddings is the causal mean above; an EmbeddingGemma-style
+ * encoder) ----
+ * Every token attends to every token of its sequence; the final-normed states
+ * are mean-pooled over the row's lens_host[b] tokens, passed through the
+ * optional dense head (tensors embed_head.dense0.weight [d, hidden] and
+ * embed_head.dense1.weight [hidden, d]) and L2-normalised into out_host
+ * [batch, hidden].  Needs a model created with prefill_path 1 (projections on
+ * the tensor cores, bf16 inputs); rows go through max_batch at a time and
+ * overwrite the model's KV cache. */
+mg_status mg_encode(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
+                    int32_t max_len, float *out_host);
+
 /* ---- inspection (tests) ---- */
 mg_status mg_read_kv(const mg_model *m, int32_t layer, int32_t row, int32_t pos, float *k_host, float *v_host);
 

@@ -125,6 +125,7 @@ _lib.mg_set_tokens.argtypes = [_P, _I32P, ctypes.c_int32]
 _lib.mg_sample.argtypes = [_F32P, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(Sampling), ctypes.c_uint64,
                            ctypes.c_uint64, _I32P]
 _lib.mg_embed.argtypes = [_P, _I32P, _I32P, ctypes.c_int32, ctypes.c_int32, _F32P]
+_lib.mg_encode.argtypes = [_P, _I32P, _I32P, ctypes.c_int32, ctypes.c_int32, _F32P]
 _lib.mg_read_kv.argtypes = [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _F32P, _F32P]
 _lib.mg_tp_ipc_handle.argtypes = [_P, _P]
 _lib.mg_tp_connect.argtypes = [_P, _P, ctypes.c_int32]
@@ -134,7 +135,7 @@ _lib.mg_trace_enable.argtypes = [_P, ctypes.c_int32]
 _lib.mg_trace_read.argtypes = [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)]
 for _f in ("mg_model_create", "mg_model_info_get", "mg_model_destroy", "mg_set_pos", "mg_get_pos", "mg_step",
            "mg_prefill", "mg_generate", "mg_set_tokens", "mg_sample", "mg_embed", "mg_read_kv",
-           "mg_tp_ipc_handle", "mg_tp_connect", "mg_tp_disconnect", "mg_trace_enable", "mg_trace_read"):
+           "mg_tp_ipc_handle", "mg_tp_connect", "mg_tp_disconnect", "mg_encode", "mg_trace_enable", "mg_trace_read"):
     getattr(_lib, _f).restype = ctypes.c_int
 
 
@@ -523,6 +524,25 @@ def generate_embeddings(llm: dict[str, Any], input_array: Any) -> npt.NDArray[np
     _check(_lib.mg_embed(h.ptr, ids.ctypes.data_as(_I32P), lens.ctypes.data_as(_I32P), len(rows), max_len,
                          out.ctypes.data_as(_F32P)))
     return _ensure_embedding_matrix(out, len(rows), hidden)
+
+
+def encode_embeddings(llm: dict[str, Any], input_array: Any) -> npt.NDArray[np.float32]:
+    """Bidirectional encoder embeddings ([batch, hidden], unit L2 norm) of ragged
+    token lists or a 2-D id array; the model must use ``prefill_path=1``."""
+    rows = [list(r) for r in input_array]
+    if not rows or any(len(r) == 0 for r in rows):
+        raise RuntimeError("inputs must contain at least one token per row")
+    max_len = max(len(r) for r in rows)
+    ids = np.zeros((len(rows), max_len), np.int32)
+    lens = np.zeros(len(rows), np.int32)
+    for i, r in enumerate(rows):
+        ids[i, : len(r)] = r
+        lens[i] = len(r)
+    out = np.zeros((len(rows), int(llm["hidden_size"])), np.float32)
+    h = _handle(llm)
+    _check(_lib.mg_encode(h.ptr, ids.ctypes.data_as(_I32P), lens.ctypes.data_as(_I32P), len(rows), max_len,
+                          out.ctypes.data_as(_F32P)))
+    return out
 
 
 def read_kv(llm: dict[str, Any], layer: int, pos: int, row: int = 0) -> tuple[np.ndarray, np.ndarray]:

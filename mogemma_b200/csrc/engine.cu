@@ -45,9 +45,12 @@ cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd
                           const int32_t *pos, float *kc, float *vc, int64_t kv_row_stride, int64_t kv_head_stride,
                           float inv_hd, cudaStream_t s);
 cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,
-                         const float *vc, const int32_t *row, const int32_t *pos, int64_t kv_row_stride,
-                         int64_t kv_head_stride, int window, int is_global, float scale, __nv_bfloat16 *out,
-                         int out_ld, cudaStream_t s);
+                         const float *vc, const int32_t *row, const int32_t *pos, const int32_t *last,
+                         int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global, float scale,
+                         __nv_bfloat16 *out, int out_ld, cudaStream_t s);
+cudaError_t pf_encoder_head(const float *x, int H, const int32_t *start, const int32_t *len, const float *final_norm,
+                            float inv_h, const float *d0, int d0_out, const float *d1, float *pool, float *mid,
+                            float *out, int B, cudaStream_t s);
 cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, cudaStream_t s);
 cudaError_t tile_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, int64_t row_off, void *dst,
                              int dst_dtype, int Kp, int rps, int mult, int kc, int nseg, int part,
@@ -153,6 +156,12 @@ struct mg_model {
     __nv_bfloat16 *pf_xn = nullptr;
     int32_t *pf_tok = nullptr, *pf_row = nullptr, *pf_pos = nullptr;
     __nv_bfloat16 *pf_lm = nullptr;  // bf16 lm_head [V][Hp] for batched decode steps
+    int32_t *pf_last = nullptr;      // encoder: last key position of each packed token
+    // encoder head (embed_head.dense0 [d][H], embed_head.dense1 [H][d]; optional)
+    float *d0 = nullptr, *d1 = nullptr;
+    int d0_out = 0;
+    float *enc_pool = nullptr, *enc_mid = nullptr, *enc_out = nullptr;
+    int32_t *enc_start = nullptr, *enc_len = nullptr;
 
     // rows: Bmax in the KV cache; Bdec the most the persistent decode kernel
     // stages (shared memory); steps with more rows take the batched path
@@ -578,6 +587,19 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     TRY(dalloc(m, reinterpret_cast<char **>(&m->embed), static_cast<size_t>(m->V_g) * m->H * we));
     TRY(upload_matrix(m, *emb, m->V_g, m->H, m->embed, wd, m->H, staging, staging_bytes));
     m->embed_ld = m->H;
+    {  // optional encoder head (this library's names for an EmbeddingGemma-style dense head)
+        const Desc *d0 = find(d, "embed_head.dense0.weight"), *d1 = find(d, "embed_head.dense1.weight");
+        if (d0 && d1 && d0->shape.size() == 2 && d1->shape.size() == 2 && d0->shape[1] == m->H &&
+            d1->shape[0] == m->H && d1->shape[1] == d0->shape[0]) {
+            m->d0_out = static_cast<int>(d0->shape[0]);
+            TRY(dalloc(m, &m->d0, static_cast<size_t>(m->d0_out) * m->H));
+            TRY(dalloc(m, &m->d1, static_cast<size_t>(m->d0_out) * m->H));
+            TRY(upload_matrix(m, *d0, m->d0_out, m->H, m->d0, MG_F32, m->H, staging, staging_bytes));
+            TRY(upload_matrix(m, *d1, m->H, m->d0_out, m->d1, MG_F32, m->d0_out, staging, staging_bytes));
+        } else if (d0 || d1) {
+            return fail(MG_ERR_INVALID, "embed_head.dense0/dense1 must be [d, hidden] and [hidden, d]");
+        }
+    }
     TRY(dalloc(m, &m->final_norm, m->H));
     TRY(upload_matrix(m, *fnorm, 1, m->H, m->final_norm, MG_F32, m->H, staging, staging_bytes));
     TRY(dalloc(m, &m->d_layers, L));
@@ -1050,6 +1072,7 @@ static mg_status pf_reserve(mg_model *m, int N) {
         TRY(dalloc(m, &m->pf_tok, cap));
         TRY(dalloc(m, &m->pf_row, cap));
         TRY(dalloc(m, &m->pf_pos, cap));
+        TRY(dalloc(m, &m->pf_last, cap));
         m->pf_cap = cap;
     }
     return MG_OK;
@@ -1057,7 +1080,7 @@ static mg_status pf_reserve(mg_model *m, int N) {
 
 // Every layer for the N tokens in pf_tok / pf_row / pf_pos: K/V into the
 // cache, and pf_xn = bf16(final-norm of the last layer's output) per token.
-static mg_status pf_layers(mg_model *m, int N) {
+static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr) {
     cudaStream_t st = m->stream;
     const float inv_h = 1.0f / static_cast<float>(m->H), inv_hd = 1.0f / static_cast<float>(m->hd);
     const float att_scale = 1.0f / sqrtf(static_cast<float>(m->hd));
@@ -1079,7 +1102,7 @@ static mg_status pf_layers(mg_model *m, int N) {
                          lp.is_global ? m->cos_g : m->cos_l, lp.is_global ? m->sin_g : m->sin_l, m->pf_row, m->pf_pos,
                          kc, vc, m->kv_row_stride, m->kv_head_stride, inv_hd, st));
         if (m->Ap > m->A) CU(cudaMemsetAsync(m->pf_xn, 0, sizeof(__nv_bfloat16) * N * m->Ap, st));
-        CU(pf_attention(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, kc, vc, m->pf_row, m->pf_pos,
+        CU(pf_attention(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, kc, vc, m->pf_row, m->pf_pos, last,
                         m->kv_row_stride, m->kv_head_stride, m->window, lp.is_global, att_scale, m->pf_xn, m->Ap, st));
         TRY(gemm(m->pf_xn, m->Ap, w.o, m->H, m->Ap, m->pf_c, m->H));
         CU(pf_resnorm(m->pf_x, m->pf_c, lp.post_attn_ln, lp.pre_ff_ln, m->pf_r, m->pf_xn, N, m->H, m->Hp, inv_h, st));
@@ -1196,6 +1219,63 @@ extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, cons
         CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice));
     }
     return st;
+}
+
+extern "C" mg_status mg_encode(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
+                               int32_t max_len, float *out_host) {
+    if (!m || !token_ids_host || !lens_host || !out_host) return fail(MG_ERR_INVALID, "null argument");
+    if (batch <= 0) return fail(MG_ERR_INVALID, "inputs must contain at least one row");
+    if (m->prefill_path != 1 || m->tp > 1)
+        return fail(MG_ERR_UNSUPPORTED, "mg_encode needs a model created with prefill_path 1 (and tp_size 1)");
+    CU(cudaSetDevice(m->dev));
+    for (int b = 0; b < batch; ++b) {
+        if (lens_host[b] <= 0 || lens_host[b] > max_len || lens_host[b] > m->cap)
+            return fail(MG_ERR_INVALID, "row %d length %d outside [1, min(max_len, capacity)]", b, lens_host[b]);
+        for (int t = 0; t < lens_host[b]; ++t) {
+            const int32_t id = token_ids_host[static_cast<int64_t>(b) * max_len + t];
+            if (id < 0 || id >= m->V_g) return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", id, m->V_g);
+        }
+    }
+    if (!m->enc_out) {
+        TRY(dalloc(m, &m->enc_pool, static_cast<size_t>(m->Bmax) * m->H));
+        TRY(dalloc(m, &m->enc_mid, static_cast<size_t>(m->Bmax) * std::max(m->d0_out, 1)));
+        TRY(dalloc(m, &m->enc_out, static_cast<size_t>(m->Bmax) * m->H));
+        TRY(dalloc(m, &m->enc_start, m->Bmax));
+        TRY(dalloc(m, &m->enc_len, m->Bmax));
+    }
+    cudaStream_t st = m->stream;
+    // sequences go through in groups of max_batch rows; their K/V use the
+    // model's cache rows at positions 0.. (the decode state is overwritten)
+    for (int b0 = 0; b0 < batch; b0 += m->Bmax) {
+        const int nb = std::min(m->Bmax, batch - b0);
+        std::vector<int32_t> tok, row, pos, last, start(nb), len(nb);
+        for (int b = 0; b < nb; ++b) {
+            const int n = lens_host[b0 + b];
+            start[b] = static_cast<int32_t>(tok.size());
+            len[b] = n;
+            for (int t = 0; t < n; ++t) {
+                tok.push_back(token_ids_host[static_cast<int64_t>(b0 + b) * max_len + t]);
+                row.push_back(b);
+                pos.push_back(t);
+                last.push_back(n - 1);
+            }
+        }
+        const int N = static_cast<int>(tok.size());
+        TRY(pf_reserve(m, N));
+        CU(cudaMemcpyAsync(m->pf_tok, tok.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+        CU(cudaMemcpyAsync(m->pf_row, row.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+        CU(cudaMemcpyAsync(m->pf_pos, pos.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+        CU(cudaMemcpyAsync(m->pf_last, last.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
+        CU(cudaMemcpyAsync(m->enc_start, start.data(), sizeof(int32_t) * nb, cudaMemcpyHostToDevice, st));
+        CU(cudaMemcpyAsync(m->enc_len, len.data(), sizeof(int32_t) * nb, cudaMemcpyHostToDevice, st));
+        TRY(pf_layers(m, N, m->pf_last));
+        CU(pf_encoder_head(m->pf_x, m->H, m->enc_start, m->enc_len, m->final_norm, 1.0f / static_cast<float>(m->H),
+                           m->d0, m->d0_out, m->d1, m->enc_pool, m->enc_mid, m->enc_out, nb, st));
+        CU(cudaMemcpyAsync(out_host + static_cast<int64_t>(b0) * m->H, m->enc_out, sizeof(float) * nb * m->H,
+                           cudaMemcpyDeviceToHost, st));
+        CU(cudaStreamSynchronize(st));  // the host vectors above are reused by the next group
+    }
+    return check_device(m);
 }
 
 extern "C" mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,

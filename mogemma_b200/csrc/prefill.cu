@@ -129,8 +129,8 @@ __global__ void __launch_bounds__(kPfThreads) pf_qk_rope_kv_kernel(
 template <int GQ>
 __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
     const float *qkv, int qkv_ld, int Hq, int Hkv, int hd, int hdp, const float *kc, const float *vc,
-    const int32_t *row, const int32_t *pos, int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global,
-    float scale, __nv_bfloat16 *out, int out_ld, int N) {
+    const int32_t *row, const int32_t *pos, const int32_t *last, int64_t kv_row_stride, int64_t kv_head_stride,
+    int window, int is_global, float scale, __nv_bfloat16 *out, int out_ld, int N) {
     constexpr int kQ = GQ > 0 ? GQ : kMaxQPerKv;
     constexpr int kDL = kMaxHeadDim / 32;
     constexpr int kW = kPfThreads / 32;
@@ -145,6 +145,13 @@ __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
     float *pl = pm + kW * gq;
     const int p = pos[n];
     const int lo = (!is_global && window > 0 && p - window + 1 > 0) ? p - window + 1 : 0;
+    // causal: keys up to the token itself; with `last` (an encoder): up to the
+    // sequence's last token, within the symmetric window on local layers
+    int hi = p;
+    if (last) {
+        hi = last[n];
+        if (!is_global && window > 0) hi = min(hi, p + window - 1);
+    }
     const float *q = qkv + n * qkv_ld + static_cast<int64_t>(kvh) * gq * hd;
     for (int i = threadIdx.x; i < gq * hd; i += kPfThreads) qs[i] = q[i];
     __syncthreads();
@@ -158,9 +165,9 @@ __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
 #pragma unroll
         for (int i = 0; i < kDL; ++i) acc[h][i] = 0.f;
     }
-    for (int t0 = lo + 32 * w; t0 <= p; t0 += 32 * kW) {
+    for (int t0 = lo + 32 * w; t0 <= hi; t0 += 32 * kW) {
         const int t = t0 + lane;
-        const bool valid = t <= p;
+        const bool valid = t <= hi;
         float s[kQ];
 #pragma unroll
         for (int h = 0; h < kQ; ++h) s[h] = 0.f;
@@ -191,7 +198,7 @@ __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
                 m[h] = m_new;
             }
         }
-        const int nb = min(32, p - t0 + 1);
+        const int nb = min(32, hi - t0 + 1);
         for (int j = 0; j < nb; ++j) {
             const float *v = vb + static_cast<int64_t>(t0 + j) * hdp;
             float vv[kDL];
@@ -258,7 +265,79 @@ __global__ void __launch_bounds__(kPfThreads) pf_geglu_kernel(const float *gu, i
     }
 }
 
+// ---- encoder head: pooling, dense layers, L2 normalisation (one CTA per sequence)
+// pool[b] = mean over the sequence's tokens [start[b], start[b] + len[b]) of
+// rmsnorm(x_t) (1 + w) (the final norm, layers.mojo:283-285), in fp32.
+__global__ void __launch_bounds__(kPfThreads) pf_pool_kernel(const float *x, int H, const int32_t *start,
+                                                             const int32_t *len, const float *w, float inv_h,
+                                                             float *pool) {
+    __shared__ float red[kPfThreads / 32];
+    const int b = blockIdx.x;
+    const float inv_n = 1.0f / static_cast<float>(len[b]);
+    // columns in blocks of 8 * kPfThreads (one block for H <= 2048; wider
+    // hidden sizes recompute each token's norm per block)
+    for (int c0 = 0; c0 < H; c0 += 8 * kPfThreads) {
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        for (int t = start[b]; t < start[b] + len[b]; ++t) {
+            const float *xt = x + static_cast<int64_t>(t) * H;
+            float s = 0.f;
+            for (int i = threadIdx.x; i < H; i += kPfThreads) s += xt[i] * xt[i];
+            const float inv = rms_inv(block_sum_pf(s, red), inv_h);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = c0 + threadIdx.x + j * kPfThreads;
+                if (i < H) acc[j] += xt[i] * inv * (1.0f + w[i]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = c0 + threadIdx.x + j * kPfThreads;
+            if (i < H) pool[static_cast<int64_t>(b) * H + i] = acc[j] * inv_n;
+        }
+    }
+}
+
+// out[b][o] = sum_k W[o][k] in[b][k] (fp32), one warp per (b, o).
+__global__ void __launch_bounds__(kPfThreads) pf_dense_kernel(const float *in, int K, const float *W, int O,
+                                                              float *out, int B) {
+    const int lane = threadIdx.x & 31;
+    const int64_t task = static_cast<int64_t>(blockIdx.x) * (kPfThreads / 32) + (threadIdx.x >> 5);
+    if (task >= static_cast<int64_t>(B) * O) return;
+    const int64_t b = task / O, o = task - b * O;
+    const float *xi = in + b * K, *wr = W + o * K;
+    float s = 0.f;
+    for (int k = lane; k < K; k += 32) s += wr[k] * xi[k];
+    s = warp_sum(s);
+    if (lane == 0) out[b * O + o] = s;
+}
+
+// row b scaled to unit L2 norm.
+__global__ void __launch_bounds__(kPfThreads) pf_l2norm_kernel(float *y, int H) {
+    __shared__ float red[kPfThreads / 32];
+    float *r = y + static_cast<int64_t>(blockIdx.x) * H;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < H; i += kPfThreads) s += r[i] * r[i];
+    const float inv = rsqrtf(fmaxf(block_sum_pf(s, red), 1e-24f));
+    for (int i = threadIdx.x; i < H; i += kPfThreads) r[i] *= inv;
+}
+
 // ---------------------------------------------------------------- launches
+cudaError_t pf_encoder_head(const float *x, int H, const int32_t *start, const int32_t *len, const float *final_norm,
+                            float inv_h, const float *d0, int d0_out, const float *d1, float *pool, float *mid,
+                            float *out, int B, cudaStream_t s) {
+    pf_pool_kernel<<<B, kPfThreads, 0, s>>>(x, H, start, len, final_norm, inv_h, d0 ? pool : out);
+    if (d0) {
+        const int w = kPfThreads / 32;
+        pf_dense_kernel<<<static_cast<int>((static_cast<int64_t>(B) * d0_out + w - 1) / w), kPfThreads, 0, s>>>(
+            pool, H, d0, d0_out, mid, B);
+        pf_dense_kernel<<<static_cast<int>((static_cast<int64_t>(B) * H + w - 1) / w), kPfThreads, 0, s>>>(
+            mid, d0_out, d1, H, out, B);
+    }
+    pf_l2norm_kernel<<<B, kPfThreads, 0, s>>>(out, H);
+    return cudaGetLastError();
+}
 cudaError_t pf_embed(const void *E, int wdtype_bf16, int64_t ld, const int32_t *tok, int N, int H, float scale,
                      float *x, cudaStream_t s) {
     if (wdtype_bf16)
@@ -282,9 +361,9 @@ cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd
     return cudaGetLastError();
 }
 cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,
-                         const float *vc, const int32_t *row, const int32_t *pos, int64_t kv_row_stride,
-                         int64_t kv_head_stride, int window, int is_global, float scale, __nv_bfloat16 *out,
-                         int out_ld, cudaStream_t s) {
+                         const float *vc, const int32_t *row, const int32_t *pos, const int32_t *last,
+                         int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global, float scale,
+                         __nv_bfloat16 *out, int out_ld, cudaStream_t s) {
     const int blocks = N * Hkv;
     const int gq = Hq / Hkv;
     const size_t smem = sizeof(float) * (static_cast<size_t>(gq) * hd * (1 + kPfThreads / 32) + 2 * (kPfThreads / 32) * gq);
@@ -297,8 +376,8 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
             if (e != cudaSuccess) return e;                                                                         \
         }                                                                                                           \
         pf_attention_kernel<G><<<blocks, kPfThreads, smem, s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, kc, vc, row, pos,   \
-                                                                kv_row_stride, kv_head_stride, window, is_global,   \
-                                                                scale, out, out_ld, N);                             \
+                                                                last, kv_row_stride, kv_head_stride, window,        \
+                                                                is_global, scale, out, out_ld, N);                  \
     } while (0)
     switch (Hq / Hkv) {
         case 1: MG_PF_ATT(1); break;

@@ -83,6 +83,8 @@ def lib() -> ctypes.CDLL:
         L.ref_step_no_logits.restype = ctypes.c_int
         L.ref_step_no_logits.argtypes = [ctypes.c_void_p, i32]
         L.ref_embed_sequence.argtypes = [ctypes.c_void_p, _I32, i64, _F, ctypes.c_int]
+        L.ref_encode_sequence.argtypes = [ctypes.c_void_p, _I32, i64, _F, i64, _F, _F]
+        L.ref_encode_sequence.restype = ctypes.c_int
         L.ref_model_k_cache.restype = _F
         L.ref_model_k_cache.argtypes = [ctypes.c_void_p]
         L.ref_model_v_cache.restype = _F
@@ -291,6 +293,20 @@ class RefModel:
         ids = np.ascontiguousarray(ids, dtype=np.int32)
         out = np.zeros(self.hidden_size, np.float32)
         lib().ref_embed_sequence(self._h, ids.ctypes.data_as(_I32), ids.size, _fp(out), int(ref_compat))
+        return out
+
+    def encode(self, ids, dense0=None, dense1=None) -> np.ndarray:
+        """Bidirectional encoder embedding (ref_encode_sequence): mean of final-normed
+        states, optional dense head ``dense0`` [d, hidden] / ``dense1`` [hidden, d], L2 norm."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.zeros(self.hidden_size, np.float32)
+        d0 = np.ascontiguousarray(dense0, dtype=np.float32) if dense0 is not None else None
+        d1 = np.ascontiguousarray(dense1, dtype=np.float32) if dense1 is not None else None
+        rc = lib().ref_encode_sequence(self._h, ids.ctypes.data_as(_I32), ids.size,
+                                       _fp(d0) if d0 is not None else None, d0.shape[0] if d0 is not None else 0,
+                                       _fp(d1) if d1 is not None else None, _fp(out))
+        if rc != 0:
+            raise ValueError("sequence length outside [1, max_seq_len]")
         return out
 
     def kv_row(self, layer: int, pos: int) -> tuple[np.ndarray, np.ndarray]:

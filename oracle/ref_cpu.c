@@ -396,3 +396,102 @@ void ref_forward_layer_raw(float *out, const float *x, const ref_layer_w *w, int
     v.sin_global = (float *)sin_t - pos * head_dim;
     forward_layer(&v, 0, out, x, pos, scratch);
 }
+
+/* Bidirectional encoder over one sequence (an EmbeddingGemma-style extension;
+ * the reference's generate_embeddings is causal, layers.mojo:292-370).  Each
+ * layer is forward_layer's arithmetic (layers.mojo:174-220) with every token
+ * attending to every token of the sequence (local layers in gemma3 mode: the
+ * symmetric window |t - s| < window).  Then the mean of the final-normed
+ * states, the dense head (d0 [d0_out][h], d1 [h][d0_out], both optional
+ * together) and L2 normalisation.  Works in freshly allocated buffers. */
+int ref_encode_sequence(ref_model *m, const int32_t *ids, int64_t n, const float *d0, int64_t d0_out,
+                        const float *d1, float *out) {
+    const int64_t H = m->h, hd = m->hd, qs = m->hq * hd, ks = m->hkv * hd, I = m->inter;
+    if (n <= 0 || n > m->max_seq) return -1;
+    float *x = (float *)calloc((size_t)(n * H), sizeof(float));
+    float *q = (float *)calloc((size_t)(n * qs), sizeof(float));
+    float *k = (float *)calloc((size_t)(n * ks), sizeof(float));
+    float *v = (float *)calloc((size_t)(n * ks), sizeof(float));
+    float *att = (float *)calloc((size_t)(n * qs), sizeof(float));
+    float *sc = (float *)calloc((size_t)n, sizeof(float));
+    float *t1 = (float *)calloc((size_t)(H > qs ? H : qs), sizeof(float));
+    /* layer frame: o, post-attn, residual, normed residual, mlp out (5H), gate, up, geglu (3I); head: 2H + d0_out */
+    float *t2 = (float *)calloc((size_t)(5 * H + 3 * I + 2 * H + d0_out), sizeof(float));
+    const float scale = 1.0f / sqrtf((float)hd);
+    for (int64_t t = 0; t < n; ++t)
+        for (int64_t i = 0; i < H; ++i) x[t * H + i] = m->embed[(int64_t)ids[t] * H + i] * sqrtf((float)H);
+    for (int l = 0; l < m->L; ++l) {
+        const ref_layer_w *w = &m->layers[l];
+        const int glob = layer_is_global(m, l);
+        const float *ct = glob ? m->cos_global : m->cos_local, *st = glob ? m->sin_global : m->sin_local;
+        for (int64_t t = 0; t < n; ++t) {
+            ref_rms_norm(t1, x + t * H, w->input_layernorm, H, 1e-6f, 16);
+            ref_vec_mat_mul(q + t * qs, t1, w->q_proj, H, qs, 16);
+            ref_vec_mat_mul(k + t * ks, t1, w->k_proj, H, ks, 16);
+            ref_vec_mat_mul(v + t * ks, t1, w->v_proj, H, ks, 16);
+            for (int64_t h = 0; h < m->hq; ++h) {
+                if (w->q_norm) ref_rms_norm(q + t * qs + h * hd, q + t * qs + h * hd, w->q_norm, hd, 1e-6f, 16);
+                ref_rope_rotate(q + t * qs + h * hd, ct + t * hd, st + t * hd, hd, 16);
+            }
+            for (int64_t h = 0; h < m->hkv; ++h) {
+                if (w->k_norm) ref_rms_norm(k + t * ks + h * hd, k + t * ks + h * hd, w->k_norm, hd, 1e-6f, 16);
+                ref_rope_rotate(k + t * ks + h * hd, ct + t * hd, st + t * hd, hd, 16);
+            }
+        }
+        for (int64_t t = 0; t < n; ++t) {
+            int64_t lo = 0, hi = n - 1;
+            if (!glob && m->mode == 1) {
+                if (t - m->window + 1 > lo) lo = t - m->window + 1;
+                if (t + m->window - 1 < hi) hi = t + m->window - 1;
+            }
+            for (int64_t h = 0; h < m->hq; ++h) {
+                const int64_t kvh = h / (m->hq / m->hkv);
+                for (int64_t s = lo; s <= hi; ++s) {
+                    float a = 0.0f;
+                    for (int64_t d = 0; d < hd; ++d) a += q[t * qs + h * hd + d] * k[s * ks + kvh * hd + d];
+                    sc[s - lo] = a * scale;
+                }
+                ref_softmax(sc, hi - lo + 1, 16);
+                float *o = att + t * qs + h * hd;
+                for (int64_t d = 0; d < hd; ++d) o[d] = 0.0f;
+                for (int64_t s = lo; s <= hi; ++s)
+                    for (int64_t d = 0; d < hd; ++d) o[d] = o[d] + sc[s - lo] * v[s * ks + kvh * hd + d];
+            }
+        }
+        for (int64_t t = 0; t < n; ++t) {
+            float *ao = t2, *pa = t2 + H, *res = t2 + 2 * H, *nr = t2 + 3 * H, *mo = t2 + 4 * H;
+            ref_vec_mat_mul(ao, att + t * qs, w->o_proj, qs, H, 16);
+            ref_rms_norm(pa, ao, w->post_attention_layernorm, H, 1e-6f, 16);
+            for (int64_t i = 0; i < H; ++i) res[i] = x[t * H + i] + pa[i];
+            ref_rms_norm(nr, res, w->pre_feedforward_layernorm, H, 1e-6f, 16);
+            float *g = mo + H, *u = g + I, *a = u + I;
+            ref_vec_mat_mul(g, nr, w->gate_proj, H, I, 16);
+            ref_vec_mat_mul(u, nr, w->up_proj, H, I, 16);
+            ref_geglu(a, g, u, I, 16);
+            ref_vec_mat_mul(mo, a, w->down_proj, I, H, 16);
+            ref_rms_norm(pa, mo, w->post_feedforward_layernorm, H, 1e-6f, 16);
+            for (int64_t i = 0; i < H; ++i) x[t * H + i] = res[i] + pa[i];
+        }
+    }
+    float *pool = t2;
+    for (int64_t i = 0; i < H; ++i) pool[i] = 0.0f;
+    for (int64_t t = 0; t < n; ++t) {
+        ref_rms_norm(t1, x + t * H, m->final_norm, H, 1e-6f, 16);
+        for (int64_t i = 0; i < H; ++i) pool[i] += t1[i];
+    }
+    for (int64_t i = 0; i < H; ++i) pool[i] /= (float)n;
+    const float *y = pool;
+    if (d0 && d1) {
+        float *h1 = t2 + H, *h2 = t2 + H + d0_out;
+        ref_vec_mat_mul(h1, pool, d0, H, d0_out, 16);
+        ref_vec_mat_mul(h2, h1, d1, d0_out, H, 16);
+        y = h2;
+    }
+    double ss = 0.0;
+    for (int64_t i = 0; i < H; ++i) ss += (double)y[i] * y[i];
+    const float inv = (float)(1.0 / sqrt(ss > 1e-24 ? ss : 1e-24));
+    for (int64_t i = 0; i < H; ++i) out[i] = y[i] * inv;
+    free(x); free(q); free(k); free(v); free(att); free(sc); free(t1); free(t2);
+    return 0;
+}
+

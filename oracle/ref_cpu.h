@@ -73,6 +73,12 @@ int ref_step_no_logits(ref_model *m, int32_t token_id);
  * scratch layout exactly (including its accumulator aliasing); 0 computes the
  * mean of final-normed states that the reference intends. */
 void ref_embed_sequence(ref_model *m, const int32_t *ids, int64_t seq_len, float *out, int ref_compat);
+/* Bidirectional encoder (EmbeddingGemma-style extension, no reference
+ * counterpart): every token attends to the whole sequence; mean of final-normed
+ * states, optional dense head d0 [d0_out][hidden] then d1 [hidden][d0_out], L2
+ * normalised into out [hidden].  Returns 0, or -1 for n outside [1, max_seq_len]. */
+int ref_encode_sequence(ref_model *m, const int32_t *ids, int64_t n, const float *d0, int64_t d0_out,
+                        const float *d1, float *out);
 /* Read back KV cache rows: [layer][pos][kv_head][head_dim] (reference layout). */
 const float *ref_model_k_cache(const ref_model *m);
 const float *ref_model_v_cache(const ref_model *m);

@@ -1,0 +1,50 @@
+"""Bidirectional encoder embeddings (mg_encode) against the oracle's ref_encode_sequence.
+
+The device path rounds the projection inputs and weights to bf16 (prefill_path 1),
+so the bound is the bf16 one of the batched prefill:
+  max |dev - ref| <= ENC_TOL * max |ref|  per row (rows are unit vectors).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from mogemma_b200 import _core, synth
+
+pytestmark = pytest.mark.gpu
+
+ENC_TOL = 2e-2
+
+
+@pytest.mark.parametrize(("mode", "head"), [(0, False), (1, True)])
+def test_encode_matches_oracle(mode: int, head: bool) -> None:
+    d = synth.tiny(window=16)
+    w = synth.make_weights(d, seed=21)
+    d0 = d1 = None
+    if head:
+        rng = np.random.default_rng(4)
+        d0 = (rng.standard_normal((384, d.hidden)) * 0.05).astype(np.float32)
+        d1 = (rng.standard_normal((d.hidden, 384)) * 0.05).astype(np.float32)
+        w["embed_head.dense0.weight"] = d0
+        w["embed_head.dense1.weight"] = d1
+    lens = [1, 17, 40, 5, 33]
+    rows = [[int(t) for t in synth.prompt_ids(n, d.vocab, seed=60 + i)] for i, n in enumerate(lens)]
+    llm = _core.init_model(synth.metadata_of(w), prefill_path=1, max_batch=2, capacity=48,
+                           mode="gemma3" if mode else "ref", sliding_window=d.window)
+    out = _core.encode_embeddings(llm, rows)
+    assert out.shape == (len(rows), d.hidden)
+    ref = oracle.RefModel(w, max_seq_len=48, mode=mode, sliding_window=d.window)
+    for b, r in enumerate(rows):
+        e = ref.encode(r, d0, d1)
+        assert float(np.max(np.abs(out[b] - e))) <= ENC_TOL * float(np.max(np.abs(e))), (b, len(r))
+        assert abs(float(np.linalg.norm(out[b])) - 1.0) < 1e-4
+
+
+def test_encode_rejects_token_path_model() -> None:
+    d = synth.tiny()
+    w = synth.make_weights(d, seed=1)
+    llm = _core.init_model(synth.metadata_of(w), capacity=16)
+    with pytest.raises(RuntimeError, match="prefill_path 1"):
+        _core.encode_embeddings(llm, [[1, 2, 3]])
