@@ -194,6 +194,111 @@ def run_prefill(args, world: int, rank: int, local: int) -> None:
         }), flush=True)
 
 
+EMBED_BATCH, EMBED_LEN, EMBED_DENSE = 256, (16, 512), 3072
+
+
+def run_embed(args, world: int, rank: int, local: int) -> None:
+    """Sequences/s of the bidirectional encoder (mg_encode): EmbeddingGemma-style
+    shape, 256 sequences with lengths uniform in [16, 512], dense 768->3072->768
+    head, L2-normalised rows.  Every N>1 rank encodes its own 256 sequences."""
+    import torch  # noqa: PLC0415
+
+    from mogemma_b200 import _core, synth  # noqa: PLC0415
+
+    d = synth.CONFIGS["embedding-300m"]
+    weights = synth.make_weights(d, seed=0)
+    rng = np.random.default_rng(7)
+    weights["embed_head.dense0.weight"] = (rng.standard_normal((EMBED_DENSE, d.hidden)) * 0.02).astype(np.float32)
+    weights["embed_head.dense1.weight"] = (rng.standard_normal((d.hidden, EMBED_DENSE)) * 0.02).astype(np.float32)
+    lens = rng.integers(EMBED_LEN[0], EMBED_LEN[1] + 1, EMBED_BATCH)
+    max_len = int(lens.max())
+    ids = np.zeros((EMBED_BATCH, max_len), np.int32)
+    for b, n in enumerate(lens):
+        ids[b, :n] = synth.prompt_ids(int(n), d.vocab, seed=100 + b)
+    lens32 = lens.astype(np.int32)
+    out = np.zeros((EMBED_BATCH, d.hidden), np.float32)
+    rows = 64  # sequences per group (the model's max_batch)
+    llm = _core.init_model(synth.metadata_of(weights), device=local, capacity=EMBED_LEN[1], max_batch=rows,
+                           prefill_path=1, mode="gemma3", sliding_window=d.window)
+    h = llm["_handle"]
+    lib = _core.lib()
+
+    def step() -> None:
+        _core._check(lib.mg_encode(h.ptr, ids.ctypes.data_as(_core._I32P), lens32.ctypes.data_as(_core._I32P),
+                                   EMBED_BATCH, max_len, out.ctypes.data_as(_core._F32P)))
+
+    for _ in range(args.warmup):
+        step()
+    stream = torch.cuda.ExternalStream(h.stream, device=torch.device("cuda", local))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        barrier(world)
+    ms = dist_max(ev0.elapsed_time(ev1), world) / args.steps
+    wall = dist_max(wall, world) / args.steps
+    tokens = int(lens.sum())
+    # tensor-core work: the projections of every token; attention (CUDA cores) and the head are listed apart
+    proj_params = d.layers * d.hidden * ((d.heads + 2 * d.kv_heads) * d.head_dim + d.heads * d.head_dim
+                                         + 3 * d.intermediate)
+    gemm_flops = 2.0 * proj_params * tokens
+    att_flops = 4.0 * d.layers * d.heads * d.head_dim * float((lens.astype(np.float64) ** 2).sum())
+    pk = peaks()
+    tf = gemm_flops / (ms / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle  # noqa: PLC0415
+
+        ref = oracle.RefModel(weights, max_seq_len=EMBED_LEN[1], mode=1, sliding_window=d.window)
+        sample = [ids[b, : lens[b]] for b in range(2)]
+        t0 = time.perf_counter()
+        for s in sample:
+            ref.encode(s, weights["embed_head.dense0.weight"], weights["embed_head.dense1.weight"])
+        dt = time.perf_counter() - t0
+        ref.close()
+        cpu = {"value": len(sample) / dt, "unit": "sequences/s", "cores": 1, "kind": "port",
+               "sample": f"2 sequences of the batch ({int(lens[0])} and {int(lens[1])} tokens) through the oracle's "
+                         "encoder on 1 host thread"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "embedding encoder sequences/s (EmbeddingGemma-style 300M, 256 sequences, lengths U[16,512])",
+            "value": world * EMBED_BATCH / (ms / 1e3), "unit": "sequences/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 (tcgen05, fp32 accumulate); attention and head fp32",
+            "data": "synthetic (seeded N(0,0.02) random-init weights, uniform random ids and lengths)",
+            "config": {"workload": f"embedding-300m encoder, {EMBED_BATCH} sequences ({tokens} tokens), lengths "
+                                   f"U[{EMBED_LEN[0]},{EMBED_LEN[1]}], dense {d.hidden}->{EMBED_DENSE}->{d.hidden}, "
+                                   f"groups of {rows} sequences", "model": "embedding-300m",
+                       "global_batch": world * EMBED_BATCH, "seq_len": EMBED_LEN[1],
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "per-step activations and weights (>1.2 GB) larger than L2"},
+            "e2e": {"value": world * EMBED_BATCH / wall, "unit": "sequences/s",
+                    "h2d_bytes_per_step": 4 * (tokens * 4 + EMBED_BATCH * 2),
+                    "d2h_bytes_per_step": 4 * EMBED_BATCH * d.hidden},
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / pk["bf16_tflops"], "peak_source": pk["source"],
+                         "kernel": "whole encoder step (projection GEMM FLOPs over the step time)",
+                         "gemm_flops_per_step": gemm_flops, "attention_flops_per_step": att_flops,
+                         "traffic": None},
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps * (EMBED_BATCH // rows) * (2 + 9 * d.layers + 4),
+        }), flush=True)
+    h.close()
+    if world > 1:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        dist.destroy_process_group()
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -284,8 +389,9 @@ def main() -> None:
     ap.add_argument("--decode", type=int, default=DECODE, help="tokens decoded per step")
     ap.add_argument("--batch", type=int, default=1,
                     help="decode rows (beyond the persistent kernel's rows: batched tensor-core steps)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="prefill: time the batched tensor-core prefill of --prompt tokens instead of the decode")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "embed"],
+                    help="prefill: the batched tensor-core prefill of --prompt tokens; embed: the bidirectional "
+                         "encoder on 256 sequences")
     ap.add_argument("--parallel", default="replicas", choices=["replicas", "tp"],
                     help="N>1: independent replicas (weak scaling) or one tensor-parallel model over the N GPUs")
     args = ap.parse_args()
@@ -296,6 +402,9 @@ def main() -> None:
         return
     if args.workload == "prefill":
         run_prefill(args, world, rank, local)
+        return
+    if args.workload == "embed":
+        run_embed(args, world, rank, local)
         return
 
     import ctypes  # noqa: PLC0415

@@ -43,7 +43,12 @@ cudaError_t pf_resnorm(const float *base, const float *add, const float *w_add, 
 cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *q_norm,
                           const float *k_norm, const float *cos_t, const float *sin_t, const int32_t *row,
                           const int32_t *pos, float *kc, float *vc, int64_t kv_row_stride, int64_t kv_head_stride,
-                          float inv_hd, cudaStream_t s);
+                          float inv_hd, __nv_bfloat16 *qb, __nv_bfloat16 *kb, __nv_bfloat16 *vt, int64_t vt_ld,
+                          cudaStream_t s);
+bool attn_tc_supported(int hd);
+cudaError_t attn_tc(const __nv_bfloat16 *qb, const __nv_bfloat16 *kb, const __nv_bfloat16 *vt, int64_t vt_ld, int N,
+                    int Hq, int Hkv, int hd, const int4 *tiles, int ntiles, int window, int bidir, float scale,
+                    __nv_bfloat16 *out, int64_t out_ld, uint32_t *err, cudaStream_t s);
 cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,
                          const float *vc, const int32_t *row, const int32_t *pos, const int32_t *last,
                          int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global, float scale,
@@ -157,6 +162,11 @@ struct mg_model {
     int32_t *pf_tok = nullptr, *pf_row = nullptr, *pf_pos = nullptr;
     __nv_bfloat16 *pf_lm = nullptr;  // bf16 lm_head [V][Hp] for batched decode steps
     int32_t *pf_last = nullptr;      // encoder: last key position of each packed token
+    // tensor-core attention operands (bf16): Q [N][Hq*hd], K [N][Hkv*hd], V^T [Hkv*hd][pf_vt_ld]
+    __nv_bfloat16 *pf_qb = nullptr, *pf_kb = nullptr, *pf_vt = nullptr;
+    int64_t pf_vt_ld = 0;
+    int4 *att_tiles = nullptr;  // {start, len, q0, 0} per 128-query tile
+    int att_tiles_cap = 0;
     // encoder head (embed_head.dense0 [d][H], embed_head.dense1 [H][d]; optional)
     float *d0 = nullptr, *d1 = nullptr;
     int d0_out = 0;
@@ -1073,6 +1083,14 @@ static mg_status pf_reserve(mg_model *m, int N) {
         TRY(dalloc(m, &m->pf_row, cap));
         TRY(dalloc(m, &m->pf_pos, cap));
         TRY(dalloc(m, &m->pf_last, cap));
+        if (attn_tc_supported(m->hd)) {
+            m->pf_vt_ld = (cap + 7) / 8 * 8;
+            TRY(dalloc(m, &m->pf_qb, static_cast<size_t>(cap) * m->Hq * m->hd));
+            TRY(dalloc(m, &m->pf_kb, static_cast<size_t>(cap) * m->Hkv * m->hd));
+            TRY(dalloc(m, &m->pf_vt, static_cast<size_t>(m->pf_vt_ld) * m->Hkv * m->hd));
+            m->att_tiles_cap = cap / 128 + m->Bmax + 1;
+            TRY(dalloc(m, &m->att_tiles, m->att_tiles_cap));
+        }
         m->pf_cap = cap;
     }
     return MG_OK;
@@ -1080,7 +1098,25 @@ static mg_status pf_reserve(mg_model *m, int N) {
 
 // Every layer for the N tokens in pf_tok / pf_row / pf_pos: K/V into the
 // cache, and pf_xn = bf16(final-norm of the last layer's output) per token.
-static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr) {
+// Upload the 128-query tiles of sequences (start, len) for the tensor-core
+// attention; returns the tile count (0: this model uses the CUDA-core kernel).
+static int upload_att_tiles(mg_model *m, const std::vector<int32_t> &start, const std::vector<int32_t> &len) {
+    if (!attn_tc_supported(m->hd) || !m->att_tiles) return 0;
+    std::vector<int4> t;
+    for (size_t b = 0; b < start.size(); ++b)
+        for (int q0 = 0; q0 < len[b]; q0 += 128) t.push_back(make_int4(start[b], len[b], q0, 0));
+    if (t.empty() || static_cast<int>(t.size()) > m->att_tiles_cap) return 0;
+    if (cudaMemcpyAsync(m->att_tiles, t.data(), sizeof(int4) * t.size(), cudaMemcpyHostToDevice, m->stream) !=
+        cudaSuccess)
+        return -1;
+    return static_cast<int>(t.size());
+}
+
+// ntiles > 0: every token's keys are tokens of this batch (sequences from
+// position 0), and the attention runs on the tensor cores over those tiles;
+// last (encoder) selects the bidirectional mask.  Otherwise the CUDA-core
+// kernel reads the KV cache (prompts that continue a cached prefix).
+static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr, int ntiles = 0) {
     cudaStream_t st = m->stream;
     const float inv_h = 1.0f / static_cast<float>(m->H), inv_hd = 1.0f / static_cast<float>(m->hd);
     const float att_scale = 1.0f / sqrtf(static_cast<float>(m->hd));
@@ -1098,12 +1134,20 @@ static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr) {
         float *kc = m->kc + static_cast<int64_t>(l) * m->kv_layer_stride;
         float *vc = m->vc + static_cast<int64_t>(l) * m->kv_layer_stride;
         TRY(gemm(m->pf_xn, m->Hp, w.qkv, m->qkv_rows, m->Hp, m->pf_c, m->qkv_rows));
+        const bool tc_att = ntiles > 0;
         CU(pf_qk_rope_kv(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, lp.q_norm, lp.k_norm,
                          lp.is_global ? m->cos_g : m->cos_l, lp.is_global ? m->sin_g : m->sin_l, m->pf_row, m->pf_pos,
-                         kc, vc, m->kv_row_stride, m->kv_head_stride, inv_hd, st));
+                         kc, vc, m->kv_row_stride, m->kv_head_stride, inv_hd, tc_att ? m->pf_qb : nullptr,
+                         tc_att ? m->pf_kb : nullptr, tc_att ? m->pf_vt : nullptr, m->pf_vt_ld, st));
         if (m->Ap > m->A) CU(cudaMemsetAsync(m->pf_xn, 0, sizeof(__nv_bfloat16) * N * m->Ap, st));
-        CU(pf_attention(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, kc, vc, m->pf_row, m->pf_pos, last,
-                        m->kv_row_stride, m->kv_head_stride, m->window, lp.is_global, att_scale, m->pf_xn, m->Ap, st));
+        if (tc_att)
+            CU(attn_tc(m->pf_qb, m->pf_kb, m->pf_vt, m->pf_vt_ld, N, m->Hq, m->Hkv, m->hd, m->att_tiles, ntiles,
+                       (!lp.is_global && m->window > 0) ? m->window : 0, last ? 1 : 0, att_scale, m->pf_xn, m->Ap,
+                       m->err, st));
+        else
+            CU(pf_attention(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, kc, vc, m->pf_row, m->pf_pos,
+                            last, m->kv_row_stride, m->kv_head_stride, m->window, lp.is_global, att_scale, m->pf_xn,
+                            m->Ap, st));
         TRY(gemm(m->pf_xn, m->Ap, w.o, m->H, m->Ap, m->pf_c, m->H));
         CU(pf_resnorm(m->pf_x, m->pf_c, lp.post_attn_ln, lp.pre_ff_ln, m->pf_r, m->pf_xn, N, m->H, m->Hp, inv_h, st));
         TRY(gemm(m->pf_xn, m->Hp, w.gu, 2 * m->I, m->Hp, m->pf_c, 2 * m->I));
@@ -1116,13 +1160,20 @@ static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr) {
 }
 
 static mg_status prefill_batched(mg_model *m, const int32_t *ids, const int32_t *lens, int batch, int max_len) {
-    std::vector<int32_t> tok, row, pos;
-    for (int b = 0; b < batch; ++b)
+    std::vector<int32_t> tok, row, pos, seq_start, seq_len;
+    bool fresh = true;  // every row starts at position 0: all keys are in this batch
+    for (int b = 0; b < batch; ++b) {
+        if (lens[b] > 0) {
+            fresh = fresh && m->h_pos[b] == 0;
+            seq_start.push_back(static_cast<int32_t>(tok.size()));
+            seq_len.push_back(lens[b]);
+        }
         for (int t = 0; t < lens[b]; ++t) {
             tok.push_back(ids[static_cast<int64_t>(b) * max_len + t]);
             row.push_back(b);
             pos.push_back(m->h_pos[b] + t);
         }
+    }
     const int N = static_cast<int>(tok.size());
     if (N == 0) return MG_OK;
     TRY(pf_reserve(m, N));
@@ -1130,7 +1181,9 @@ static mg_status prefill_batched(mg_model *m, const int32_t *ids, const int32_t 
     CU(cudaMemcpyAsync(m->pf_tok, tok.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
     CU(cudaMemcpyAsync(m->pf_row, row.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
     CU(cudaMemcpyAsync(m->pf_pos, pos.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
-    return pf_layers(m, N);
+    const int ntiles = fresh ? upload_att_tiles(m, seq_start, seq_len) : 0;
+    if (ntiles < 0) return fail(MG_ERR_CUDA, "tile upload failed");
+    return pf_layers(m, N, nullptr, ntiles);
 }
 
 // One decode step for rows [0, batch) on the batched path (more rows than the
@@ -1268,7 +1321,9 @@ extern "C" mg_status mg_encode(mg_model *m, const int32_t *token_ids_host, const
         CU(cudaMemcpyAsync(m->pf_last, last.data(), sizeof(int32_t) * N, cudaMemcpyHostToDevice, st));
         CU(cudaMemcpyAsync(m->enc_start, start.data(), sizeof(int32_t) * nb, cudaMemcpyHostToDevice, st));
         CU(cudaMemcpyAsync(m->enc_len, len.data(), sizeof(int32_t) * nb, cudaMemcpyHostToDevice, st));
-        TRY(pf_layers(m, N, m->pf_last));
+        const int ntiles = upload_att_tiles(m, start, len);
+        if (ntiles < 0) return fail(MG_ERR_CUDA, "tile upload failed");
+        TRY(pf_layers(m, N, m->pf_last, ntiles));
         CU(pf_encoder_head(m->pf_x, m->H, m->enc_start, m->enc_len, m->final_norm, 1.0f / static_cast<float>(m->H),
                            m->d0, m->d0_out, m->d1, m->enc_pool, m->enc_mid, m->enc_out, nb, st));
         CU(cudaMemcpyAsync(out_host + static_cast<int64_t>(b0) * m->H, m->enc_out, sizeof(float) * nb * m->H,

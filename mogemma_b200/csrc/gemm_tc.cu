@@ -25,6 +25,7 @@
 
 #include "../../include/mogemma_b200.h"
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace mg {
 mg_status report_error(mg_status st, const char *msg);
@@ -42,49 +43,7 @@ constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * (kABytes + kBByte
 constexpr uint32_t kTmemCols = 128;
 constexpr uint32_t kErrTcFull = 0x21000000u, kErrTcEmpty = 0x22000000u, kErrTcDone = 0x23000000u;
 
-// Instruction descriptor (kind::f16): D f32 (bits 4-5 = 1), A bf16 (7-9 = 1),
-// B bf16 (10-12 = 1), both K-major (15, 16 = 0), N >> 3 at 17-22, M >> 4 at 24-28.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(kBN) >> 3) << 17) |
-                            ((static_cast<uint32_t>(kBM) >> 4) << 24);
-
-// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle
-// layout that the TMA writes: rows 128 bytes apart, 8-row groups 1024 bytes
-// apart (stride byte offset), descriptor version 1, layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
-           (2ull << 61);
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            dst),
-        "l"(map), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %4, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(kIdesc)
-        : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
+constexpr uint32_t kIdesc = idesc_bf16(kBM, kBN);
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -134,7 +93,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t a0 = sa + s * kABytes, b0 = sb + s * kBBytes;
 #pragma unroll
             for (int k = 0; k < kBK / kUK; ++k)
-                umma_bf16(tmem, sw128_desc(a0 + k * kUK * 2), sw128_desc(b0 + k * kUK * 2), (kt | k) != 0 ? 1u : 0u);
+                umma_bf16(tmem, sw128_desc(a0 + k * kUK * 2), sw128_desc(b0 + k * kUK * 2), kIdesc, (kt | k) != 0 ? 1u : 0u);
             umma_commit(smem_u32(&empty[s]));
         }
         umma_commit(smem_u32(&done));  // arrives once every MMA issued above has completed
@@ -163,36 +122,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
-// ---------------------------------------------------------------- host
-using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiled encode_fn() {
-    static EncodeTiled fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(p);
-    });
-    return fn;
-}
-
-// [rows][K] bf16 with row stride ld elements; boxes of 64 x box_rows, 128-byte swizzle.
-static bool make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, int64_t ld, int box_rows) {
-    EncodeTiled fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 }  // namespace tc
 
 // C[M][N] = A[M][K] . B[N][K]^T; A, B bf16 device memory (16-byte aligned rows),
@@ -208,7 +137,7 @@ cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb,
         attr = true;
     }
     CUtensorMap ma, mb;
-    if (!make_map(&ma, A, M, K, lda, kBM) || !make_map(&mb, B, N, K, ldb, kBN)) return cudaErrorInvalidValue;
+    if (!make_map_bf16(&ma, A, M, K, lda, kBM) || !make_map_bf16(&mb, B, N, K, ldb, kBN)) return cudaErrorInvalidValue;
     const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
     gemm_bf16_tc_kernel<<<grid, kThreads, kSmem, stream>>>(ma, mb, C, M, N, K, ldc, err);
     return cudaGetLastError();

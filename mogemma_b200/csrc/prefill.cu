@@ -83,7 +83,8 @@ __global__ void __launch_bounds__(kPfThreads) pf_resnorm_kernel(const float *bas
 __global__ void __launch_bounds__(kPfThreads) pf_qk_rope_kv_kernel(
     float *qkv, int qkv_ld, int Hq, int Hkv, int hd, int hdp, const float *q_norm, const float *k_norm,
     const float *cos_t, const float *sin_t, const int32_t *row, const int32_t *pos, float *kc, float *vc,
-    int64_t kv_row_stride, int64_t kv_head_stride, float inv_hd) {
+    int64_t kv_row_stride, int64_t kv_head_stride, float inv_hd, __nv_bfloat16 *qb, __nv_bfloat16 *kb,
+    __nv_bfloat16 *vt, int64_t vt_ld) {
     const int64_t n = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int half = hd / 2;
@@ -115,6 +116,14 @@ __global__ void __launch_bounds__(kPfThreads) pf_qk_rope_kv_kernel(
                 kc[off + d] = x[d];
                 vc[off + d] = v[d];
             }
+            if (kb) {  // bf16 operands of the tensor-core attention: K by token, V transposed
+                for (int d = lane; d < hd; d += 32) {
+                    kb[(n * Hkv + kvh) * hd + d] = __float2bfloat16_rn(x[d]);
+                    vt[(static_cast<int64_t>(kvh) * hd + d) * vt_ld + n] = __float2bfloat16_rn(v[d]);
+                }
+            }
+        } else if (qb) {
+            for (int d = lane; d < hd; d += 32) qb[(n * Hq + vec) * hd + d] = __float2bfloat16_rn(x[d]);
         }
     }
 }
@@ -355,9 +364,11 @@ cudaError_t pf_resnorm(const float *base, const float *add, const float *w_add, 
 cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *q_norm,
                           const float *k_norm, const float *cos_t, const float *sin_t, const int32_t *row,
                           const int32_t *pos, float *kc, float *vc, int64_t kv_row_stride, int64_t kv_head_stride,
-                          float inv_hd, cudaStream_t s) {
+                          float inv_hd, __nv_bfloat16 *qb, __nv_bfloat16 *kb, __nv_bfloat16 *vt, int64_t vt_ld,
+                          cudaStream_t s) {
     pf_qk_rope_kv_kernel<<<N, kPfThreads, 0, s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, q_norm, k_norm, cos_t, sin_t, row,
-                                                    pos, kc, vc, kv_row_stride, kv_head_stride, inv_hd);
+                                                    pos, kc, vc, kv_row_stride, kv_head_stride, inv_hd, qb, kb, vt,
+                                                    vt_ld);
     return cudaGetLastError();
 }
 cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,

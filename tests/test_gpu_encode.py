@@ -18,9 +18,16 @@ pytestmark = pytest.mark.gpu
 ENC_TOL = 2e-2
 
 
-@pytest.mark.parametrize(("mode", "head"), [(0, False), (1, True)])
-def test_encode_matches_oracle(mode: int, head: bool) -> None:
-    d = synth.tiny(window=16)
+@pytest.mark.parametrize(("mode", "head", "lens", "hd"), [(0, False, (1, 17, 40, 5, 33), 64),
+                                                         (1, True, (1, 17, 40, 5, 33), 64),
+                                                         (1, False, (300, 129, 7), 64), (0, True, (257, 64), 64),
+                                                         (1, True, (200, 3, 61), 128), (1, False, (150, 20), 256),
+                                                         (0, False, (140,), 256)])
+def test_encode_matches_oracle(mode: int, head: bool, lens: tuple[int, ...], hd: int) -> None:
+    """Short rows (one key block), and rows over several 128-query tiles and
+    128-key blocks, with the 16-token window on local layers in mode 1; head
+    dims 64, 128 and 256 (each a tensor-core attention instantiation)."""
+    d = synth.tiny(window=16, head_dim=hd)
     w = synth.make_weights(d, seed=21)
     d0 = d1 = None
     if head:
@@ -29,13 +36,12 @@ def test_encode_matches_oracle(mode: int, head: bool) -> None:
         d1 = (rng.standard_normal((d.hidden, 384)) * 0.05).astype(np.float32)
         w["embed_head.dense0.weight"] = d0
         w["embed_head.dense1.weight"] = d1
-    lens = [1, 17, 40, 5, 33]
     rows = [[int(t) for t in synth.prompt_ids(n, d.vocab, seed=60 + i)] for i, n in enumerate(lens)]
-    llm = _core.init_model(synth.metadata_of(w), prefill_path=1, max_batch=2, capacity=48,
+    llm = _core.init_model(synth.metadata_of(w), prefill_path=1, max_batch=2, capacity=max(lens) + 8,
                            mode="gemma3" if mode else "ref", sliding_window=d.window)
     out = _core.encode_embeddings(llm, rows)
     assert out.shape == (len(rows), d.hidden)
-    ref = oracle.RefModel(w, max_seq_len=48, mode=mode, sliding_window=d.window)
+    ref = oracle.RefModel(w, max_seq_len=max(lens) + 8, mode=mode, sliding_window=d.window)
     for b, r in enumerate(rows):
         e = ref.encode(r, d0, d1)
         assert float(np.max(np.abs(out[b] - e))) <= ENC_TOL * float(np.max(np.abs(e))), (b, len(r))

@@ -41,11 +41,29 @@ def _check(dims: synth.Gemma3Dims, prompt_len: int, *, mode: int = 0, seed: int 
     return {"logit_err": float(np.max(np.abs(dev - r))) / float(np.max(np.abs(r))), "kv_err": kv_err}
 
 
-@pytest.mark.parametrize(("prompt_len", "mode"), [(37, 0), (130, 0), (70, 1)])
-def test_batched_prefill_matches_oracle(prompt_len: int, mode: int) -> None:
-    res = _check(synth.tiny(window=32), prompt_len, mode=mode)
+@pytest.mark.parametrize(("prompt_len", "mode", "hd"), [(37, 0, 64), (130, 0, 64), (70, 1, 64), (300, 1, 64),
+                                                       (389, 0, 64), (260, 1, 256), (150, 0, 128)])
+def test_batched_prefill_matches_oracle(prompt_len: int, mode: int, hd: int) -> None:
+    res = _check(synth.tiny(window=32, head_dim=hd), prompt_len, mode=mode)
     print(res)
     assert res["kv_err"] <= PF_TOL and res["logit_err"] <= PF_TOL, res
+
+
+def test_prefill_continuing_a_cached_prefix() -> None:
+    """A second prefill call continues the row from position 40: its keys
+    include cached positions, which the CUDA-core attention reads."""
+    d = synth.tiny(window=32)
+    w = synth.make_weights(d, seed=17)
+    toks = [int(t) for t in synth.prompt_ids(181, d.vocab, seed=5)]
+    llm = _core.init_model(synth.metadata_of(w), prefill_path=1, capacity=192, mode="gemma3", sliding_window=d.window)
+    _core.prefill(llm, toks[:40])
+    _core.prefill(llm, toks[40:180])
+    ref = oracle.RefModel(w, max_seq_len=192, mode=1, sliding_window=d.window)
+    for t in toks[:180]:
+        ref.step_no_logits(t)
+    dev = _core.step(llm, toks[180], 0.0, 0, 1.0)
+    r = ref.step(toks[180])
+    assert float(np.max(np.abs(dev - r))) <= PF_TOL * float(np.max(np.abs(r)))
 
 
 def test_batched_prefill_rows() -> None:
