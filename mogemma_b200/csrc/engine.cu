@@ -53,9 +53,9 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
                          const float *vc, const int32_t *row, const int32_t *pos, const int32_t *last,
                          int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global, float scale,
                          __nv_bfloat16 *out, int out_ld, cudaStream_t s);
-cudaError_t pf_encoder_head(const float *x, int H, const int32_t *start, const int32_t *len, const float *final_norm,
-                            float inv_h, const float *d0, int d0_out, const float *d1, float *pool, float *mid,
-                            float *out, int B, cudaStream_t s);
+cudaError_t pf_encoder_head(const float *x, int H, int N, const int32_t *start, const int32_t *len,
+                            const float *final_norm, float inv_h, float *row_inv, const float *d0, int d0_out,
+                            const float *d1, float *pool, float *mid, float *out, int B, cudaStream_t s);
 cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, cudaStream_t s);
 cudaError_t tile_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, int64_t row_off, void *dst,
                              int dst_dtype, int Kp, int rps, int mult, int kc, int nseg, int part,
@@ -1324,8 +1324,9 @@ extern "C" mg_status mg_encode(mg_model *m, const int32_t *token_ids_host, const
         const int ntiles = upload_att_tiles(m, start, len);
         if (ntiles < 0) return fail(MG_ERR_CUDA, "tile upload failed");
         TRY(pf_layers(m, N, m->pf_last, ntiles));
-        CU(pf_encoder_head(m->pf_x, m->H, m->enc_start, m->enc_len, m->final_norm, 1.0f / static_cast<float>(m->H),
-                           m->d0, m->d0_out, m->d1, m->enc_pool, m->enc_mid, m->enc_out, nb, st));
+        // per-token 1/rms goes into pf_r (free after the last layer)
+        CU(pf_encoder_head(m->pf_x, m->H, N, m->enc_start, m->enc_len, m->final_norm, 1.0f / static_cast<float>(m->H),
+                           m->pf_r, m->d0, m->d0_out, m->d1, m->enc_pool, m->enc_mid, m->enc_out, nb, st));
         CU(cudaMemcpyAsync(out_host + static_cast<int64_t>(b0) * m->H, m->enc_out, sizeof(float) * nb * m->H,
                            cudaMemcpyDeviceToHost, st));
         CU(cudaStreamSynchronize(st));  // the host vectors above are reused by the next group

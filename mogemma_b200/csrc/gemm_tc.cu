@@ -35,7 +35,7 @@ constexpr int kBM = 128;   // tile rows (TMEM lanes)
 constexpr int kBN = 128;   // tile columns (TMEM columns)
 constexpr int kBK = 64;    // K per stage: 64 bf16 = 128 bytes, one swizzle row
 constexpr int kUK = 16;    // K of one tcgen05.mma (kind::f16)
-constexpr int kStages = 4;
+constexpr int kStages = 3;  // 97 KB of shared memory: two CTAs per SM, one's epilogue under the other's MMAs
 constexpr int kThreads = 128;
 constexpr uint32_t kABytes = kBM * kBK * 2;
 constexpr uint32_t kBBytes = kBN * kBK * 2;
@@ -45,7 +45,7 @@ constexpr uint32_t kErrTcFull = 0x21000000u, kErrTcEmpty = 0x22000000u, kErrTcDo
 
 constexpr uint32_t kIdesc = idesc_bf16(kBM, kBN);
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         float *C, int M, int N, int K, int64_t ldc, uint32_t *err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -100,21 +100,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
 
-    // epilogue: warp w owns TMEM lanes (tile rows) 32w .. 32w + 31
+    // epilogue: warp w owns TMEM lanes (tile rows) 32w .. 32w + 31.  Each 32 x 32
+    // block goes through shared memory (the ring is free once `done` fired; a
+    // padded [32][33] float tile per warp) so that every global store of the
+    // warp writes 32 consecutive floats of one row.
     const bool have = mbar_wait(&done, 0u, err, kErrTcDone);
     tc_fence_after();
-    const int row = m0 + warp * 32 + lane;
     // tcgen05.ld is warp-collective: decide per warp
     if (__all_sync(0xffffffffu, have && ld_relaxed_u32(err) == 0u)) {
+        float *stage = reinterpret_cast<float *>(base) + warp * 32 * 33;
+        const int row0 = m0 + warp * 32;
         for (int c0 = 0; c0 < kBN; c0 += 32) {
             uint32_t v[32];
             tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(c0), v);
-            if (row < M) {
-                float *dst = C + static_cast<int64_t>(row) * ldc + n0 + c0;
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (n0 + c0 + j < N) dst[j] = __uint_as_float(v[j]);
+            for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = __uint_as_float(v[j]);
+            __syncwarp();
+            const int col = n0 + c0 + lane;
+            if (col < N) {
+                const int rows = min(32, M - row0);
+#pragma unroll 4
+                for (int rr = 0; rr < rows; ++rr) C[static_cast<int64_t>(row0 + rr) * ldc + col] = stage[rr * 33 + lane];
             }
+            __syncwarp();
         }
     }
     tc_fence_before();

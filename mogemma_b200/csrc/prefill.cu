@@ -77,20 +77,74 @@ __global__ void __launch_bounds__(kPfThreads) pf_resnorm_kernel(const float *bas
         xn[n * Kp + i] = __float2bfloat16_rn(i < H ? res[n * H + i] * inv * (1.0f + w_next[i]) : 0.f);
 }
 
+// The same, one warp per token (8 tokens per CTA), float4 loads; H and Kp multiples of 4.
+__global__ void __launch_bounds__(kPfThreads) pf_resnorm_warp_kernel(const float *base, const float *add,
+                                                                     const float *w_add, const float *w_next,
+                                                                     float *res, __nv_bfloat16 *xn, int H, int Kp,
+                                                                     float inv_h, int N) {
+    const int lane = threadIdx.x & 31;
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * (kPfThreads / 32) + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const int H4 = H / 4;
+    const float4 *b4 = reinterpret_cast<const float4 *>(base + n * H);
+    const float4 *a4 = add ? reinterpret_cast<const float4 *>(add + n * H) : nullptr;
+    float4 *r4 = reinterpret_cast<float4 *>(res + n * H);
+    float inv_a = 0.f;
+    if (add) {
+        float s = 0.f;
+        for (int i = lane; i < H4; i += 32) {
+            const float4 v = a4[i];
+            s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        inv_a = rms_inv(warp_sum(s), inv_h);
+    }
+    float s2 = 0.f;
+    for (int i = lane; i < H4; i += 32) {
+        float4 x = b4[i];
+        if (add) {
+            const float4 a = a4[i], w = reinterpret_cast<const float4 *>(w_add)[i];
+            x.x += a.x * inv_a * (1.0f + w.x);
+            x.y += a.y * inv_a * (1.0f + w.y);
+            x.z += a.z * inv_a * (1.0f + w.z);
+            x.w += a.w * inv_a * (1.0f + w.w);
+        }
+        r4[i] = x;
+        s2 += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+    }
+    const float inv = rms_inv(warp_sum(s2), inv_h);
+    for (int i = lane; i < Kp / 4; i += 32) {
+        float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < H4) {
+            const float4 x = r4[i], w = reinterpret_cast<const float4 *>(w_next)[i];
+            y = make_float4(x.x * inv * (1.0f + w.x), x.y * inv * (1.0f + w.y), x.z * inv * (1.0f + w.z),
+                            x.w * inv * (1.0f + w.w));
+        }
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(y.x, y.y), hi = __floats2bfloat162_rn(y.z, y.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t *>(&lo);
+        pk.y = *reinterpret_cast<const uint32_t *>(&hi);
+        reinterpret_cast<uint2 *>(xn + n * Kp)[i] = pk;
+    }
+}
+
 // QK-norm (layers.mojo:43-49) and RoPE (52-55) of each token's q heads (in
 // place) and k head(s); k and v into the KV cache at (row, pos) (57-61).
-// One CTA per token, one warp per head vector.
+// One warp per (token, head vector), 8 per CTA.
 __global__ void __launch_bounds__(kPfThreads) pf_qk_rope_kv_kernel(
     float *qkv, int qkv_ld, int Hq, int Hkv, int hd, int hdp, const float *q_norm, const float *k_norm,
     const float *cos_t, const float *sin_t, const int32_t *row, const int32_t *pos, float *kc, float *vc,
     int64_t kv_row_stride, int64_t kv_head_stride, float inv_hd, __nv_bfloat16 *qb, __nv_bfloat16 *kb,
-    __nv_bfloat16 *vt, int64_t vt_ld) {
-    const int64_t n = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __nv_bfloat16 *vt, int64_t vt_ld, int N) {
+    const int lane = threadIdx.x & 31;
+    const int nv = Hq + Hkv;
+    const int64_t item = static_cast<int64_t>(blockIdx.x) * (kPfThreads / 32) + (threadIdx.x >> 5);
+    if (item >= static_cast<int64_t>(N) * nv) return;
+    const int64_t n = item / nv;
     const int half = hd / 2;
     const int p = pos[n];
     float *x0 = qkv + n * qkv_ld;
-    for (int vec = warp; vec < Hq + Hkv; vec += kPfThreads / 32) {
+    {
+        const int vec = static_cast<int>(item - n * nv);
         float *x = x0 + static_cast<int64_t>(vec) * hd;  // q heads then k heads (layout of the qkv rows)
         const float *nw = vec < Hq ? q_norm : k_norm;
         if (nw) {
@@ -263,8 +317,8 @@ __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
 // act = bf16(gelu_erf(gate) * up) (ops.mojo:5-30); gu rows hold [gate (I) | up (I)].
 __global__ void __launch_bounds__(kPfThreads) pf_geglu_kernel(const float *gu, int I, int gu_ld, __nv_bfloat16 *act,
                                                               int Ip) {
-    const int64_t n = blockIdx.y;
-    for (int i = blockIdx.x * kPfThreads + threadIdx.x; i < Ip; i += gridDim.x * kPfThreads) {
+    const int64_t n = blockIdx.x;
+    for (int i = blockIdx.y * kPfThreads + threadIdx.x; i < Ip; i += gridDim.y * kPfThreads) {
         float a = 0.f;
         if (i < I) {
             const float g = gu[n * gu_ld + i], u = gu[n * gu_ld + I + i];
@@ -273,39 +327,52 @@ __global__ void __launch_bounds__(kPfThreads) pf_geglu_kernel(const float *gu, i
         act[n * Ip + i] = __float2bfloat16_rn(a);
     }
 }
-
-// ---- encoder head: pooling, dense layers, L2 normalisation (one CTA per sequence)
-// pool[b] = mean over the sequence's tokens [start[b], start[b] + len[b]) of
-// rmsnorm(x_t) (1 + w) (the final norm, layers.mojo:283-285), in fp32.
-__global__ void __launch_bounds__(kPfThreads) pf_pool_kernel(const float *x, int H, const int32_t *start,
-                                                             const int32_t *len, const float *w, float inv_h,
-                                                             float *pool) {
-    __shared__ float red[kPfThreads / 32];
-    const int b = blockIdx.x;
-    const float inv_n = 1.0f / static_cast<float>(len[b]);
-    // columns in blocks of 8 * kPfThreads (one block for H <= 2048; wider
-    // hidden sizes recompute each token's norm per block)
-    for (int c0 = 0; c0 < H; c0 += 8 * kPfThreads) {
-        float acc[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-        for (int t = start[b]; t < start[b] + len[b]; ++t) {
-            const float *xt = x + static_cast<int64_t>(t) * H;
-            float s = 0.f;
-            for (int i = threadIdx.x; i < H; i += kPfThreads) s += xt[i] * xt[i];
-            const float inv = rms_inv(block_sum_pf(s, red), inv_h);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = c0 + threadIdx.x + j * kPfThreads;
-                if (i < H) acc[j] += xt[i] * inv * (1.0f + w[i]);
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int i = c0 + threadIdx.x + j * kPfThreads;
-            if (i < H) pool[static_cast<int64_t>(b) * H + i] = acc[j] * inv_n;
-        }
+// The same, 4 features per thread (I, Ip and gu_ld multiples of 4).
+__global__ void __launch_bounds__(kPfThreads) pf_geglu4_kernel(const float *gu, int I, int gu_ld, __nv_bfloat16 *act,
+                                                               int Ip) {
+    const int64_t n = blockIdx.x;
+    const int i = 4 * (blockIdx.y * kPfThreads + threadIdx.x);
+    if (i >= Ip) return;
+    float r[4] = {0.f, 0.f, 0.f, 0.f};
+    if (i < I) {
+        const float4 g = *reinterpret_cast<const float4 *>(gu + n * gu_ld + i);
+        const float4 u = *reinterpret_cast<const float4 *>(gu + n * gu_ld + I + i);
+        r[0] = 0.5f * g.x * (1.0f + erff(g.x * kInvSqrt2)) * u.x;
+        r[1] = 0.5f * g.y * (1.0f + erff(g.y * kInvSqrt2)) * u.y;
+        r[2] = 0.5f * g.z * (1.0f + erff(g.z * kInvSqrt2)) * u.z;
+        r[3] = 0.5f * g.w * (1.0f + erff(g.w * kInvSqrt2)) * u.w;
     }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(r[0], r[1]), hi = __floats2bfloat162_rn(r[2], r[3]);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t *>(&lo);
+    pk.y = *reinterpret_cast<const uint32_t *>(&hi);
+    *reinterpret_cast<uint2 *>(act + n * Ip + i) = pk;
+}
+
+// ---- encoder head: pooling, dense layers, L2 normalisation
+// inv[t] = 1 / rms(x_t) over the packed tokens, one warp per token.
+__global__ void __launch_bounds__(kPfThreads) pf_rowinv_kernel(const float *x, int H, float inv_h, float *inv,
+                                                               int N) {
+    const int t = blockIdx.x * (kPfThreads / 32) + (threadIdx.x >> 5);
+    if (t >= N) return;
+    const float *xt = x + static_cast<int64_t>(t) * H;
+    float s = 0.f;
+    for (int i = threadIdx.x & 31; i < H; i += 32) s += xt[i] * xt[i];
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) inv[t] = rms_inv(s, inv_h);
+}
+// pool[b][i] = mean over the sequence's tokens [start[b], start[b] + len[b]) of
+// x_t[i] inv[t] (1 + w[i]) -- the final norm (layers.mojo:283-285) then the
+// mean, in fp32.  Grid (sequences, column blocks of kPfThreads).
+__global__ void __launch_bounds__(kPfThreads) pf_pool_kernel(const float *x, int H, const int32_t *start,
+                                                             const int32_t *len, const float *w, const float *inv,
+                                                             float *pool) {
+    const int b = blockIdx.x;
+    const int i = blockIdx.y * kPfThreads + threadIdx.x;
+    if (i >= H) return;
+    float acc = 0.f;
+    for (int t = start[b]; t < start[b] + len[b]; ++t) acc += x[static_cast<int64_t>(t) * H + i] * inv[t];
+    pool[static_cast<int64_t>(b) * H + i] = acc * (1.0f + w[i]) / static_cast<float>(len[b]);
 }
 
 // out[b][o] = sum_k W[o][k] in[b][k] (fp32), one warp per (b, o).
@@ -333,10 +400,13 @@ __global__ void __launch_bounds__(kPfThreads) pf_l2norm_kernel(float *y, int H) 
 }
 
 // ---------------------------------------------------------------- launches
-cudaError_t pf_encoder_head(const float *x, int H, const int32_t *start, const int32_t *len, const float *final_norm,
-                            float inv_h, const float *d0, int d0_out, const float *d1, float *pool, float *mid,
-                            float *out, int B, cudaStream_t s) {
-    pf_pool_kernel<<<B, kPfThreads, 0, s>>>(x, H, start, len, final_norm, inv_h, d0 ? pool : out);
+cudaError_t pf_encoder_head(const float *x, int H, int N, const int32_t *start, const int32_t *len,
+                            const float *final_norm, float inv_h, float *row_inv, const float *d0, int d0_out,
+                            const float *d1, float *pool, float *mid, float *out, int B, cudaStream_t s) {
+    constexpr int wpb = kPfThreads / 32;
+    pf_rowinv_kernel<<<(N + wpb - 1) / wpb, kPfThreads, 0, s>>>(x, H, inv_h, row_inv, N);
+    pf_pool_kernel<<<dim3(B, (H + kPfThreads - 1) / kPfThreads), kPfThreads, 0, s>>>(x, H, start, len, final_norm,
+                                                                                       row_inv, d0 ? pool : out);
     if (d0) {
         const int w = kPfThreads / 32;
         pf_dense_kernel<<<static_cast<int>((static_cast<int64_t>(B) * d0_out + w - 1) / w), kPfThreads, 0, s>>>(
@@ -358,7 +428,11 @@ cudaError_t pf_embed(const void *E, int wdtype_bf16, int64_t ld, const int32_t *
 }
 cudaError_t pf_resnorm(const float *base, const float *add, const float *w_add, const float *w_next, float *res,
                        __nv_bfloat16 *xn, int N, int H, int Kp, float inv_h, cudaStream_t s) {
-    pf_resnorm_kernel<<<N, kPfThreads, 0, s>>>(base, add, w_add, w_next, res, xn, H, Kp, inv_h);
+    if (H % 4 == 0 && Kp % 4 == 0)
+        pf_resnorm_warp_kernel<<<(N + kPfThreads / 32 - 1) / (kPfThreads / 32), kPfThreads, 0, s>>>(
+            base, add, w_add, w_next, res, xn, H, Kp, inv_h, N);
+    else
+        pf_resnorm_kernel<<<N, kPfThreads, 0, s>>>(base, add, w_add, w_next, res, xn, H, Kp, inv_h);
     return cudaGetLastError();
 }
 cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *q_norm,
@@ -366,9 +440,11 @@ cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd
                           const int32_t *pos, float *kc, float *vc, int64_t kv_row_stride, int64_t kv_head_stride,
                           float inv_hd, __nv_bfloat16 *qb, __nv_bfloat16 *kb, __nv_bfloat16 *vt, int64_t vt_ld,
                           cudaStream_t s) {
-    pf_qk_rope_kv_kernel<<<N, kPfThreads, 0, s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, q_norm, k_norm, cos_t, sin_t, row,
+    const int64_t items = static_cast<int64_t>(N) * (Hq + Hkv);
+    pf_qk_rope_kv_kernel<<<static_cast<unsigned>((items + kPfThreads / 32 - 1) / (kPfThreads / 32)), kPfThreads, 0,
+                           s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, q_norm, k_norm, cos_t, sin_t, row,
                                                     pos, kc, vc, kv_row_stride, kv_head_stride, inv_hd, qb, kb, vt,
-                                                    vt_ld);
+                                                    vt_ld, N);
     return cudaGetLastError();
 }
 cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,
@@ -400,8 +476,10 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
     return cudaGetLastError();
 }
 cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, cudaStream_t s) {
-    const dim3 grid((Ip + kPfThreads - 1) / kPfThreads, N);
-    pf_geglu_kernel<<<grid, kPfThreads, 0, s>>>(gu, I, gu_ld, act, Ip);
+    if (I % 4 == 0 && Ip % 4 == 0 && gu_ld % 4 == 0)
+        pf_geglu4_kernel<<<dim3(N, (Ip / 4 + kPfThreads - 1) / kPfThreads), kPfThreads, 0, s>>>(gu, I, gu_ld, act, Ip);
+    else
+        pf_geglu_kernel<<<dim3(N, (Ip + kPfThreads - 1) / kPfThreads), kPfThreads, 0, s>>>(gu, I, gu_ld, act, Ip);
     return cudaGetLastError();
 }
 
