@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -132,19 +133,172 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 }  // namespace tc
 
+namespace tc {
+// ---- persistent variant for grids with at least one 128 x 256 tile per SM:
+// one CTA per SM walks the tiles.
+//  * warp 0, one lane: TMA producer over a 4-stage ring (128 x 64 A + 256 x 64 B per stage);
+//  * warp 1: allocates 512 TMEM columns = two 256-column fp32 accumulators; one
+//    lane issues tcgen05.mma (M=128, N=256, K=16) into the free accumulator and
+//    commits it to acc_full when the tile's K loop is issued;
+//  * warps 2-5: epilogue of the other accumulator (warp w reads TMEM lanes
+//    32 (w % 4) ..), staged through a padded [32][33] float tile per warp so
+//    every store of a warp writes 32 consecutive floats of one row; then the
+//    accumulator is handed back (acc_empty).
+// So a tile's epilogue runs under the next tile's MMAs.
+constexpr int kPBN = 256;
+constexpr int kPStages = 4;
+constexpr int kPThreads = 192;
+constexpr uint32_t kPABytes = kBM * kBK * 2;
+constexpr uint32_t kPBBytes = kPBN * kBK * 2;
+constexpr size_t kPSmem = 1024 + static_cast<size_t>(kPStages) * (kPABytes + kPBBytes) + 4 * 32 * 33 * 4;
+constexpr uint32_t kPTmemCols = 512;
+constexpr uint32_t kPIdesc = idesc_bf16(kBM, kPBN);
+constexpr uint32_t kErrTcAcc = 0x2A000000u;
+
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_bf16_tc_persistent_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                                   float *C, int M, int N, int K, int64_t ldc, uint32_t *err) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full[kPStages], empty[kPStages], acc_full[2], acc_empty[2];
+    __shared__ uint32_t tmem_slot;
+    const uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
+    const uint32_t sa = smem_u32(reinterpret_cast<void *>(base));
+    const uint32_t sb = sa + kPStages * kPABytes;
+    float *stage_all = reinterpret_cast<float *>(base + kPStages * (kPABytes + kPBBytes));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (N + kPBN - 1) / kPBN;
+    const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
+    const int nk = K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"(kPTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kPBN;
+                for (int kt = 0; kt < nk; ++kt, ++it) {
+                    const uint32_t s = it % kPStages;
+                    if (it >= kPStages && !mbar_wait(&empty[s], ((it / kPStages) - 1) & 1u, err, kErrTcEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], kPABytes + kPBBytes);
+                    tma_load_2d(sa + s * kPABytes, &map_a, kt * kBK, m0, smem_u32(&full[s]));
+                    tma_load_2d(sb + s * kPBBytes, &map_b, kt * kBK, n0, smem_u32(&full[s]));
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t it = 0, i = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++i) {
+                const uint32_t b = i & 1u;
+                if (i >= 2 && !mbar_wait(&acc_empty[b], ((i >> 1) - 1) & 1u, err, kErrTcAcc)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + b * kPBN;
+                for (int kt = 0; kt < nk; ++kt, ++it) {
+                    const uint32_t s = it % kPStages;
+                    if (!mbar_wait(&full[s], (it / kPStages) & 1u, err, kErrTcFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = sa + s * kPABytes, b0 = sb + s * kPBBytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / kUK; ++k)
+                        umma_bf16(acc, sw128_desc(a0 + k * kUK * 2), sw128_desc(b0 + k * kUK * 2), kPIdesc,
+                                  (kt | k) != 0 ? 1u : 0u);
+                    umma_commit(smem_u32(&empty[s]));
+                }
+                if (ok) umma_commit(smem_u32(&acc_full[b]));
+            }
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quadrant this warp may read
+        float *stage = stage_all + (warp - 2) * 32 * 33;
+        uint32_t i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+            const uint32_t b = i & 1u;
+            const bool ok = mbar_wait(&acc_full[b], (i >> 1) & 1u, err, kErrTcDone);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kPBN;
+            const int row0 = m0 + q * 32;
+            const int rows = min(32, M - row0);
+            for (int c0 = 0; c0 < kPBN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kPBN + static_cast<uint32_t>(c0), v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = __uint_as_float(v[j]);
+                __syncwarp();
+                const int col = n0 + c0 + lane;
+                if (col < N) {
+#pragma unroll 4
+                    for (int rr = 0; rr < rows; ++rr)
+                        C[static_cast<int64_t>(row0 + rr) * ldc + col] = stage[rr * 33 + lane];
+                }
+                __syncwarp();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPTmemCols));
+}
+}  // namespace tc
+
 // C[M][N] = A[M][K] . B[N][K]^T; A, B bf16 device memory (16-byte aligned rows),
 // K a multiple of 64, err a device word that receives a code on a timeout.
 cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb, float *C, int64_t ldc, int M, int N,
                          int K, uint32_t *err, cudaStream_t stream) {
     using namespace tc;
-    static bool attr = false;
-    if (!attr) {
+    static int sms = 0;
+    if (sms == 0) {
         cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmem));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_bf16_tc_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kPSmem));
+        int dev = 0;
+        if (e == cudaSuccess) e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
-        attr = true;
     }
     CUtensorMap ma, mb;
+    const int ntiles = ((M + kBM - 1) / kBM) * ((N + kPBN - 1) / kPBN);
+    if (ntiles >= sms) {  // enough 128 x 256 tiles to fill every SM: the persistent kernel
+        if (!make_map_bf16(&ma, A, M, K, lda, kBM) || !make_map_bf16(&mb, B, N, K, ldb, kPBN))
+            return cudaErrorInvalidValue;
+        gemm_bf16_tc_persistent_kernel<<<std::min(ntiles, sms), kPThreads, kPSmem, stream>>>(ma, mb, C, M, N, K, ldc,
+                                                                                          err);
+        return cudaGetLastError();
+    }
     if (!make_map_bf16(&ma, A, M, K, lda, kBM) || !make_map_bf16(&mb, B, N, K, ldb, kBN)) return cudaErrorInvalidValue;
     const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
     gemm_bf16_tc_kernel<<<grid, kThreads, kSmem, stream>>>(ma, mb, C, M, N, K, ldc, err);

@@ -34,8 +34,12 @@ def _gemm(torch, a, b, n_cols=None):
     return c
 
 
+# Fewer 128 x 256 tiles than SMs: one 128 x 128 tile per CTA; otherwise the
+# persistent kernel (128 x 256 tiles, two TMEM accumulators), here with several
+# tiles per CTA (288, 320 and 160 tiles on 148 SMs) and ragged rows / columns.
 @pytest.mark.parametrize(("M", "N", "K"), [(128, 128, 64), (256, 384, 1152), (300, 700, 512), (1, 1536, 1152),
-                                           (513, 129, 6912)])
+                                           (513, 129, 6912), (4096, 2304, 768), (8191, 1280, 1152),
+                                           (5000, 1000, 256)])
 def test_gemm_matches_fp32_product(M: int, N: int, K: int) -> None:
     torch = pytest.importorskip("torch")
     g = torch.Generator(device="cpu").manual_seed(M * 7 + N)
