@@ -186,8 +186,9 @@ mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const int32_t *le
  * optional dense head (tensors embed_head.dense0.weight [d, hidden] and
  * embed_head.dense1.weight [hidden, d]) and L2-normalised into out_host
  * [batch, hidden].  Needs a model created with prefill_path 1 (projections on
- * the tensor cores, bf16 inputs); rows go through max_batch at a time and
- * overwrite the model's KV cache. */
+ * the tensor cores, bf16 inputs); rows go through max_batch at a time.  The
+ * model's KV cache may be overwritten (head dims other than 64/128/256 run
+ * the attention from the cache): treat its decode state as lost. */
 mg_status mg_encode(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
                     int32_t max_len, float *out_host);
 

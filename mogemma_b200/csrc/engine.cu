@@ -56,7 +56,9 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
 cudaError_t pf_encoder_head(const float *x, int H, int N, const int32_t *start, const int32_t *len,
                             const float *final_norm, float inv_h, float *row_inv, const float *d0, int d0_out,
                             const float *d1, float *pool, float *mid, float *out, int B, cudaStream_t s);
-cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, cudaStream_t s);
+cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, int il, cudaStream_t s);
+cudaError_t gemm_bf16_tc_geglu(const void *A, int64_t lda, const void *B, int64_t ldb, __nv_bfloat16 *act,
+                               int64_t ld_act, int M, int N2, int K, uint32_t *err, cudaStream_t stream);
 cudaError_t tile_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, int64_t row_off, void *dst,
                              int dst_dtype, int Kp, int rps, int mult, int kc, int nseg, int part,
                              cudaStream_t stream);
@@ -156,6 +158,8 @@ struct mg_model {
         __nv_bfloat16 *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
     };
     std::vector<PfLayer> pf;
+    bool gu_il = false;               // PfLayer::gu rows in alternating 128-row gate / up blocks
+    __nv_bfloat16 *pf_act = nullptr;  // [cap][Ip] GeGLU output of the fused gate/up GEMM
     int pf_cap = 0, pf_kx = 0, pf_cx = 0;
     float *pf_x = nullptr, *pf_r = nullptr, *pf_c = nullptr;
     __nv_bfloat16 *pf_xn = nullptr;
@@ -575,10 +579,22 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
                               pl.qkv + static_cast<size_t>(m->A + kvr) * m->Hp, MG_BF16, m->Hp, staging, staging_bytes));
             TRY(upload_matrix(m, *lw(l, "self_attn.o_proj.weight"), m->H, m->A, pl.o, MG_BF16, m->Ap, staging,
                               staging_bytes));
-            TRY(upload_matrix(m, *lw(l, "mlp.gate_proj.weight"), m->I, m->H, pl.gu, MG_BF16, m->Hp, staging,
-                              staging_bytes));
-            TRY(upload_matrix(m, *lw(l, "mlp.up_proj.weight"), m->I, m->H, pl.gu + static_cast<size_t>(m->I) * m->Hp,
-                              MG_BF16, m->Hp, staging, staging_bytes));
+            m->gu_il = m->I % 128 == 0;
+            if (m->gu_il) {  // 128 gate rows, then the same features' 128 up rows, ...
+                for (int64_t f0 = 0; f0 < m->I; f0 += 128) {
+                    TRY(upload_matrix(m, rows_view(*lw(l, "mlp.gate_proj.weight"), f0), 128, m->H,
+                                      pl.gu + static_cast<size_t>(2 * f0) * m->Hp, MG_BF16, m->Hp, staging,
+                                      staging_bytes));
+                    TRY(upload_matrix(m, rows_view(*lw(l, "mlp.up_proj.weight"), f0), 128, m->H,
+                                      pl.gu + static_cast<size_t>(2 * f0 + 128) * m->Hp, MG_BF16, m->Hp, staging,
+                                      staging_bytes));
+                }
+            } else {
+                TRY(upload_matrix(m, *lw(l, "mlp.gate_proj.weight"), m->I, m->H, pl.gu, MG_BF16, m->Hp, staging,
+                                  staging_bytes));
+                TRY(upload_matrix(m, *lw(l, "mlp.up_proj.weight"), m->I, m->H,
+                                  pl.gu + static_cast<size_t>(m->I) * m->Hp, MG_BF16, m->Hp, staging, staging_bytes));
+            }
             TRY(upload_matrix(m, *lw(l, "mlp.down_proj.weight"), m->H, m->I, pl.down, MG_BF16, m->Ip, staging,
                               staging_bytes));
             m->pf.push_back(pl);
@@ -1083,6 +1099,7 @@ static mg_status pf_reserve(mg_model *m, int N) {
         TRY(dalloc(m, &m->pf_row, cap));
         TRY(dalloc(m, &m->pf_pos, cap));
         TRY(dalloc(m, &m->pf_last, cap));
+        if (m->gu_il) TRY(dalloc(m, &m->pf_act, static_cast<size_t>(cap) * m->Ip));
         if (attn_tc_supported(m->hd)) {
             m->pf_vt_ld = (cap + 7) / 8 * 8;
             TRY(dalloc(m, &m->pf_qb, static_cast<size_t>(cap) * m->Hq * m->hd));
@@ -1135,9 +1152,12 @@ static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr, in
         float *vc = m->vc + static_cast<int64_t>(l) * m->kv_layer_stride;
         TRY(gemm(m->pf_xn, m->Hp, w.qkv, m->qkv_rows, m->Hp, m->pf_c, m->qkv_rows));
         const bool tc_att = ntiles > 0;
+        // an encoder pass on the tensor cores reads no cache: K / V stay out of it
+        const bool to_cache = !(tc_att && last);
         CU(pf_qk_rope_kv(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, lp.q_norm, lp.k_norm,
                          lp.is_global ? m->cos_g : m->cos_l, lp.is_global ? m->sin_g : m->sin_l, m->pf_row, m->pf_pos,
-                         kc, vc, m->kv_row_stride, m->kv_head_stride, inv_hd, tc_att ? m->pf_qb : nullptr,
+                         to_cache ? kc : nullptr, to_cache ? vc : nullptr, m->kv_row_stride, m->kv_head_stride,
+                         inv_hd, tc_att ? m->pf_qb : nullptr,
                          tc_att ? m->pf_kb : nullptr, tc_att ? m->pf_vt : nullptr, m->pf_vt_ld, st));
         if (m->Ap > m->A) CU(cudaMemsetAsync(m->pf_xn, 0, sizeof(__nv_bfloat16) * N * m->Ap, st));
         if (tc_att)
@@ -1150,9 +1170,20 @@ static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr, in
                             m->Ap, st));
         TRY(gemm(m->pf_xn, m->Ap, w.o, m->H, m->Ap, m->pf_c, m->H));
         CU(pf_resnorm(m->pf_x, m->pf_c, lp.post_attn_ln, lp.pre_ff_ln, m->pf_r, m->pf_xn, N, m->H, m->Hp, inv_h, st));
-        TRY(gemm(m->pf_xn, m->Hp, w.gu, 2 * m->I, m->Hp, m->pf_c, 2 * m->I));
-        CU(pf_geglu(m->pf_c, m->I, 2 * m->I, m->pf_xn, m->Ip, N, st));
-        TRY(gemm(m->pf_xn, m->Ip, w.down, m->H, m->Ip, m->pf_c, m->H));
+        // gate/up + GeGLU: fused into the GEMM epilogue when the grid fills the GPU
+        const __nv_bfloat16 *act = m->pf_xn;
+        const cudaError_t fe = m->gu_il ? gemm_bf16_tc_geglu(m->pf_xn, m->Hp, w.gu, m->Hp, m->pf_act, m->Ip, N,
+                                                             2 * m->I, m->Hp, m->err, st)
+                                        : cudaErrorNotSupported;
+        if (fe == cudaSuccess) {
+            act = m->pf_act;
+        } else if (fe == cudaErrorNotSupported) {
+            TRY(gemm(m->pf_xn, m->Hp, w.gu, 2 * m->I, m->Hp, m->pf_c, 2 * m->I));
+            CU(pf_geglu(m->pf_c, m->I, 2 * m->I, m->pf_xn, m->Ip, N, m->gu_il ? 1 : 0, st));
+        } else {
+            CU(fe);
+        }
+        TRY(gemm(act, m->Ip, w.down, m->H, m->Ip, m->pf_c, m->H));
         const float *w_next = l + 1 < m->L ? m->h_layers[l + 1].in_ln : m->final_norm;
         CU(pf_resnorm(m->pf_r, m->pf_c, lp.post_ff_ln, w_next, m->pf_x, m->pf_xn, N, m->H, m->Hp, inv_h, st));
     }

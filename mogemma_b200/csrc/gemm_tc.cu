@@ -145,6 +145,11 @@ namespace tc {
 //    every store of a warp writes 32 consecutive floats of one row; then the
 //    accumulator is handed back (acc_empty).
 // So a tile's epilogue runs under the next tile's MMAs.
+// GEGLU: B holds gate and up rows in alternating blocks of 128 (rows
+// 256 j .. 256 j + 127 gate features 128 j .., the next 128 the up rows of the
+// same features), so each tile has both halves of 128 features and the
+// epilogue writes act[m][128 j + c] = bf16(gelu_erf(gate) * up) (ops.mojo:5-30)
+// instead of the fp32 products.
 constexpr int kPBN = 256;
 constexpr int kPStages = 4;
 constexpr int kPThreads = 192;
@@ -155,9 +160,10 @@ constexpr uint32_t kPTmemCols = 512;
 constexpr uint32_t kPIdesc = idesc_bf16(kBM, kPBN);
 constexpr uint32_t kErrTcAcc = 0x2A000000u;
 
+template <bool GEGLU>
 __global__ void __launch_bounds__(kPThreads, 1)
     gemm_bf16_tc_persistent_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                                   float *C, int M, int N, int K, int64_t ldc, uint32_t *err) {
+                                   float *C, __nv_bfloat16 *act, int M, int N, int K, int64_t ldc, uint32_t *err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[kPStages], empty[kPStages], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
@@ -248,19 +254,41 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kPBN;
             const int row0 = m0 + q * 32;
             const int rows = min(32, M - row0);
-            for (int c0 = 0; c0 < kPBN; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kPBN + static_cast<uint32_t>(c0), v);
+            const uint32_t t_acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kPBN;
+            if constexpr (GEGLU) {
+                for (int c0 = 0; c0 < kPBN / 2; c0 += 32) {
+                    uint32_t g[32], u[32];
+                    tmem_ld32(t_acc + static_cast<uint32_t>(c0), g);
+                    tmem_ld32(t_acc + static_cast<uint32_t>(kPBN / 2 + c0), u);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = __uint_as_float(v[j]);
-                __syncwarp();
-                const int col = n0 + c0 + lane;
-                if (col < N) {
+                    for (int j = 0; j < 32; ++j) {
+                        const float gv = __uint_as_float(g[j]);
+                        stage[lane * 33 + j] = 0.5f * gv * (1.0f + erff(gv * kInvSqrt2)) * __uint_as_float(u[j]);
+                    }
+                    __syncwarp();
+                    const int f = n0 / 2 + c0 + lane;
+                    if (f < N / 2) {
 #pragma unroll 4
-                    for (int rr = 0; rr < rows; ++rr)
-                        C[static_cast<int64_t>(row0 + rr) * ldc + col] = stage[rr * 33 + lane];
+                        for (int rr = 0; rr < rows; ++rr)
+                            act[static_cast<int64_t>(row0 + rr) * ldc + f] = __float2bfloat16_rn(stage[rr * 33 + lane]);
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
+            } else {
+                for (int c0 = 0; c0 < kPBN; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(t_acc + static_cast<uint32_t>(c0), v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = __uint_as_float(v[j]);
+                    __syncwarp();
+                    const int col = n0 + c0 + lane;
+                    if (col < N) {
+#pragma unroll 4
+                        for (int rr = 0; rr < rows; ++rr)
+                            C[static_cast<int64_t>(row0 + rr) * ldc + col] = stage[rr * 33 + lane];
+                    }
+                    __syncwarp();
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -273,35 +301,65 @@ __global__ void __launch_bounds__(kPThreads, 1)
 }
 }  // namespace tc
 
+namespace tc {
+static int g_sms = 0;  // SM count of the device, set with the kernels' shared-memory limits
+
+static cudaError_t gemm_setup() {
+    if (g_sms != 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_bf16_tc_persistent_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kPSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_bf16_tc_persistent_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kPSmem));
+    int dev = 0, sms = 0;
+    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) g_sms = sms;
+    return e;
+}
+}  // namespace tc
+
 // C[M][N] = A[M][K] . B[N][K]^T; A, B bf16 device memory (16-byte aligned rows),
 // K a multiple of 64, err a device word that receives a code on a timeout.
 cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb, float *C, int64_t ldc, int M, int N,
                          int K, uint32_t *err, cudaStream_t stream) {
     using namespace tc;
-    static int sms = 0;
-    if (sms == 0) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmem));
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_bf16_tc_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kPSmem));
-        int dev = 0;
-        if (e == cudaSuccess) e = cudaGetDevice(&dev);
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-    }
+    const cudaError_t e = gemm_setup();
+    if (e != cudaSuccess) return e;
     CUtensorMap ma, mb;
     const int ntiles = ((M + kBM - 1) / kBM) * ((N + kPBN - 1) / kPBN);
-    if (ntiles >= sms) {  // enough 128 x 256 tiles to fill every SM: the persistent kernel
+    if (ntiles >= g_sms) {  // enough 128 x 256 tiles to fill every SM: the persistent kernel
         if (!make_map_bf16(&ma, A, M, K, lda, kBM) || !make_map_bf16(&mb, B, N, K, ldb, kPBN))
             return cudaErrorInvalidValue;
-        gemm_bf16_tc_persistent_kernel<<<std::min(ntiles, sms), kPThreads, kPSmem, stream>>>(ma, mb, C, M, N, K, ldc,
-                                                                                          err);
+        gemm_bf16_tc_persistent_kernel<false><<<std::min(ntiles, g_sms), kPThreads, kPSmem, stream>>>(
+            ma, mb, C, nullptr, M, N, K, ldc, err);
         return cudaGetLastError();
     }
     if (!make_map_bf16(&ma, A, M, K, lda, kBM) || !make_map_bf16(&mb, B, N, K, ldb, kBN)) return cudaErrorInvalidValue;
     const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
     gemm_bf16_tc_kernel<<<grid, kThreads, kSmem, stream>>>(ma, mb, C, M, N, K, ldc, err);
+    return cudaGetLastError();
+}
+
+// act[M][N2/2] (bf16, row stride ld_act) = GeGLU of A . B^T with B's rows in
+// alternating 128-row gate / up blocks (N2 a multiple of 256).  Returns
+// cudaErrorNotSupported, launching nothing, when the grid has fewer tiles
+// than SMs; the caller then takes the fp32 product and a separate GeGLU.
+cudaError_t gemm_bf16_tc_geglu(const void *A, int64_t lda, const void *B, int64_t ldb, __nv_bfloat16 *act,
+                               int64_t ld_act, int M, int N2, int K, uint32_t *err, cudaStream_t stream) {
+    using namespace tc;
+    const cudaError_t e = gemm_setup();
+    if (e != cudaSuccess) return e;
+    const int ntiles = ((M + kBM - 1) / kBM) * (N2 / kPBN);
+    if (N2 % kPBN != 0 || ntiles < g_sms) return cudaErrorNotSupported;
+    CUtensorMap ma, mb;
+    if (!make_map_bf16(&ma, A, M, K, lda, kBM) || !make_map_bf16(&mb, B, N2, K, ldb, kPBN))
+        return cudaErrorInvalidValue;
+    gemm_bf16_tc_persistent_kernel<true><<<std::min(ntiles, g_sms), kPThreads, kPSmem, stream>>>(
+        ma, mb, nullptr, act, M, N2, K, ld_act, err);
     return cudaGetLastError();
 }
 

@@ -182,6 +182,93 @@ __global__ void __launch_bounds__(kPfThreads) pf_qk_rope_kv_kernel(
     }
 }
 
+// The same for head dims 64 / 128 / 256 with each head vector in registers
+// (lane holds dims lane + 32 i; the RoPE partner d + hd/2 is in the same lane).
+// Writes only what the attention that follows reads: q / k back into qkv and
+// K / V into the cache (kc non-null) for the CUDA-core attention or a later
+// decode step, bf16 Q and K (qb, kb non-null) for the tensor-core attention.
+template <int HD>
+__global__ void __launch_bounds__(kPfThreads) pf_qk_rope_reg_kernel(
+    float *qkv, int qkv_ld, int Hq, int Hkv, int hdp, const float *q_norm, const float *k_norm, const float *cos_t,
+    const float *sin_t, const int32_t *row, const int32_t *pos, float *kc, float *vc, int64_t kv_row_stride,
+    int64_t kv_head_stride, float inv_hd, int write_back, __nv_bfloat16 *qb, __nv_bfloat16 *kb, int N) {
+    constexpr int kR = HD / 32, kHalf = HD / 2, kP = kR / 2;
+    const int lane = threadIdx.x & 31;
+    const int nv = Hq + Hkv;
+    const int64_t item = static_cast<int64_t>(blockIdx.x) * (kPfThreads / 32) + (threadIdx.x >> 5);
+    if (item >= static_cast<int64_t>(N) * nv) return;
+    const int64_t n = item / nv;
+    const int vec = static_cast<int>(item - n * nv);
+    const int p = pos[n];
+    float *x0 = qkv + n * qkv_ld;
+    float *xg = x0 + static_cast<int64_t>(vec) * HD;  // q heads then k heads (layout of the qkv rows)
+    float x[kR];
+#pragma unroll
+    for (int i = 0; i < kR; ++i) x[i] = xg[lane + 32 * i];
+    const float *nw = vec < Hq ? q_norm : k_norm;
+    if (nw) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < kR; ++i) ss += x[i] * x[i];
+        const float inv = rms_inv(warp_sum(ss), inv_hd);
+#pragma unroll
+        for (int i = 0; i < kR; ++i) x[i] = x[i] * inv * (1.0f + nw[lane + 32 * i]);
+    }
+    const float *c = cos_t + static_cast<int64_t>(p) * kHalf;
+    const float *sn = sin_t + static_cast<int64_t>(p) * kHalf;
+#pragma unroll
+    for (int i = 0; i < kP; ++i) {
+        const float cc = c[lane + 32 * i], ss = sn[lane + 32 * i];
+        const float x1 = x[i], x2 = x[i + kP];
+        x[i] = x1 * cc - x2 * ss;
+        x[i + kP] = x2 * cc + x1 * ss;
+    }
+    if (write_back) {
+#pragma unroll
+        for (int i = 0; i < kR; ++i) xg[lane + 32 * i] = x[i];
+    }
+    if (vec >= Hq) {
+        const int kvh = vec - Hq;
+        if (kc) {
+            const int64_t off = row[n] * kv_row_stride + kvh * kv_head_stride + static_cast<int64_t>(p) * hdp;
+            const float *v = x0 + static_cast<int64_t>(Hq + Hkv + kvh) * HD;
+#pragma unroll
+            for (int i = 0; i < kR; ++i) {
+                kc[off + lane + 32 * i] = x[i];
+                vc[off + lane + 32 * i] = v[lane + 32 * i];
+            }
+        }
+        if (kb) {
+#pragma unroll
+            for (int i = 0; i < kR; ++i) kb[(n * Hkv + kvh) * HD + lane + 32 * i] = __float2bfloat16_rn(x[i]);
+        }
+    } else if (qb) {
+#pragma unroll
+        for (int i = 0; i < kR; ++i) qb[(n * Hq + vec) * HD + lane + 32 * i] = __float2bfloat16_rn(x[i]);
+    }
+}
+
+// vt[c][n] = bf16(V[n][c]) for the packed tokens (V = the v part of the qkv
+// rows, c over Hkv * hd): 32 x 32 tiles through shared memory, so both the
+// reads (along c) and the writes (along n) are coalesced.
+__global__ void __launch_bounds__(kPfThreads) pf_v_transpose_kernel(const float *qkv, int qkv_ld, int v_off, int C,
+                                                                    __nv_bfloat16 *vt, int64_t vt_ld, int N) {
+    __shared__ float tile[32][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+    const int n0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+#pragma unroll
+    for (int r = ty; r < 32; r += kPfThreads / 32) {
+        const int n = n0 + r, c = c0 + tx;
+        tile[r][tx] = (n < N && c < C) ? qkv[static_cast<int64_t>(n) * qkv_ld + v_off + c] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = ty; r < 32; r += kPfThreads / 32) {
+        const int c = c0 + r, n = n0 + tx;
+        if (c < C && n < N) vt[static_cast<int64_t>(c) * vt_ld + n] = __float2bfloat16_rn(tile[tx][r]);
+    }
+}
+
 // Causal attention over the cached positions lo..pos (layers.mojo:63-94).  One
 // CTA per (token, kv head) for its GQ q heads (each K/V row read once for the
 // group); its 8 warps take interleaved blocks of 32 keys, one key per lane:
@@ -315,13 +402,18 @@ __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
 }
 
 // act = bf16(gelu_erf(gate) * up) (ops.mojo:5-30); gu rows hold [gate (I) | up (I)].
+// il: gate and up columns in alternating blocks of 128 (feature f at column
+// 256 (f / 128) + f % 128, its up value 128 further) instead of [gate | up].
+__device__ __forceinline__ int geglu_gate_col(int f, int il) { return il ? ((f & ~127) << 1) + (f & 127) : f; }
+
 __global__ void __launch_bounds__(kPfThreads) pf_geglu_kernel(const float *gu, int I, int gu_ld, __nv_bfloat16 *act,
-                                                              int Ip) {
+                                                              int Ip, int il) {
     const int64_t n = blockIdx.x;
     for (int i = blockIdx.y * kPfThreads + threadIdx.x; i < Ip; i += gridDim.y * kPfThreads) {
         float a = 0.f;
         if (i < I) {
-            const float g = gu[n * gu_ld + i], u = gu[n * gu_ld + I + i];
+            const int gc = geglu_gate_col(i, il), uc = il ? gc + 128 : I + i;
+            const float g = gu[n * gu_ld + gc], u = gu[n * gu_ld + uc];
             a = 0.5f * g * (1.0f + erff(g * kInvSqrt2)) * u;
         }
         act[n * Ip + i] = __float2bfloat16_rn(a);
@@ -329,14 +421,15 @@ __global__ void __launch_bounds__(kPfThreads) pf_geglu_kernel(const float *gu, i
 }
 // The same, 4 features per thread (I, Ip and gu_ld multiples of 4).
 __global__ void __launch_bounds__(kPfThreads) pf_geglu4_kernel(const float *gu, int I, int gu_ld, __nv_bfloat16 *act,
-                                                               int Ip) {
+                                                               int Ip, int il) {
     const int64_t n = blockIdx.x;
     const int i = 4 * (blockIdx.y * kPfThreads + threadIdx.x);
     if (i >= Ip) return;
     float r[4] = {0.f, 0.f, 0.f, 0.f};
     if (i < I) {
-        const float4 g = *reinterpret_cast<const float4 *>(gu + n * gu_ld + i);
-        const float4 u = *reinterpret_cast<const float4 *>(gu + n * gu_ld + I + i);
+        const int gc = geglu_gate_col(i, il), uc = il ? gc + 128 : I + i;  // 4 features stay in one block
+        const float4 g = *reinterpret_cast<const float4 *>(gu + n * gu_ld + gc);
+        const float4 u = *reinterpret_cast<const float4 *>(gu + n * gu_ld + uc);
         r[0] = 0.5f * g.x * (1.0f + erff(g.x * kInvSqrt2)) * u.x;
         r[1] = 0.5f * g.y * (1.0f + erff(g.y * kInvSqrt2)) * u.y;
         r[2] = 0.5f * g.z * (1.0f + erff(g.z * kInvSqrt2)) * u.z;
@@ -435,12 +528,34 @@ cudaError_t pf_resnorm(const float *base, const float *add, const float *w_add, 
         pf_resnorm_kernel<<<N, kPfThreads, 0, s>>>(base, add, w_add, w_next, res, xn, H, Kp, inv_h);
     return cudaGetLastError();
 }
+// q/k norm + RoPE, the cache write (kc null: skipped; only for the
+// tensor-core attention of an encoder pass) and the bf16 operands of the
+// tensor-core attention (qb null: none, and q / k go back into qkv for the
+// CUDA-core attention).
 cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *q_norm,
                           const float *k_norm, const float *cos_t, const float *sin_t, const int32_t *row,
                           const int32_t *pos, float *kc, float *vc, int64_t kv_row_stride, int64_t kv_head_stride,
                           float inv_hd, __nv_bfloat16 *qb, __nv_bfloat16 *kb, __nv_bfloat16 *vt, int64_t vt_ld,
                           cudaStream_t s) {
     const int64_t items = static_cast<int64_t>(N) * (Hq + Hkv);
+    const unsigned blocks = static_cast<unsigned>((items + kPfThreads / 32 - 1) / (kPfThreads / 32));
+    if (hd == 64 || hd == 128 || hd == 256) {
+        const int write_back = qb ? 0 : 1;
+#define MG_PF_ROPE(HD)                                                                                            \
+    pf_qk_rope_reg_kernel<HD><<<blocks, kPfThreads, 0, s>>>(qkv, qkv_ld, Hq, Hkv, hdp, q_norm, k_norm, cos_t,     \
+                                                            sin_t, row, pos, kc, vc, kv_row_stride,             \
+                                                            kv_head_stride, inv_hd, write_back, qb, kb, N)
+        if (hd == 64) MG_PF_ROPE(64);
+        else if (hd == 128) MG_PF_ROPE(128);
+        else MG_PF_ROPE(256);
+#undef MG_PF_ROPE
+        if (vt) {
+            const dim3 g((N + 31) / 32, (Hkv * hd + 31) / 32);
+            pf_v_transpose_kernel<<<g, kPfThreads, 0, s>>>(qkv, qkv_ld, (Hq + Hkv) * hd, Hkv * hd, vt, vt_ld, N);
+        }
+        return cudaGetLastError();
+    }
+    if (!kc) return cudaErrorInvalidValue;  // the generic kernel always fills the cache
     pf_qk_rope_kv_kernel<<<static_cast<unsigned>((items + kPfThreads / 32 - 1) / (kPfThreads / 32)), kPfThreads, 0,
                            s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, q_norm, k_norm, cos_t, sin_t, row,
                                                     pos, kc, vc, kv_row_stride, kv_head_stride, inv_hd, qb, kb, vt,
@@ -475,11 +590,12 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
 #undef MG_PF_ATT
     return cudaGetLastError();
 }
-cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, cudaStream_t s) {
+cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, int il, cudaStream_t s) {
     if (I % 4 == 0 && Ip % 4 == 0 && gu_ld % 4 == 0)
-        pf_geglu4_kernel<<<dim3(N, (Ip / 4 + kPfThreads - 1) / kPfThreads), kPfThreads, 0, s>>>(gu, I, gu_ld, act, Ip);
+        pf_geglu4_kernel<<<dim3(N, (Ip / 4 + kPfThreads - 1) / kPfThreads), kPfThreads, 0, s>>>(gu, I, gu_ld, act, Ip,
+                                                                                               il);
     else
-        pf_geglu_kernel<<<dim3(N, (Ip + kPfThreads - 1) / kPfThreads), kPfThreads, 0, s>>>(gu, I, gu_ld, act, Ip);
+        pf_geglu_kernel<<<dim3(N, (Ip + kPfThreads - 1) / kPfThreads), kPfThreads, 0, s>>>(gu, I, gu_ld, act, Ip, il);
     return cudaGetLastError();
 }
 

@@ -22,12 +22,14 @@ ENC_TOL = 2e-2
                                                          (1, True, (1, 17, 40, 5, 33), 64),
                                                          (1, False, (300, 129, 7), 64), (0, True, (257, 64), 64),
                                                          (1, True, (200, 3, 61), 128), (1, False, (150, 20), 256),
-                                                         (0, False, (140,), 256)])
+                                                         (0, False, (140,), 256), (1, True, (600, 100), 4096)])
 def test_encode_matches_oracle(mode: int, head: bool, lens: tuple[int, ...], hd: int) -> None:
     """Short rows (one key block), and rows over several 128-query tiles and
     128-key blocks, with the 16-token window on local layers in mode 1; head
-    dims 64, 128 and 256 (each a tensor-core attention instantiation)."""
-    d = synth.tiny(window=16, head_dim=hd)
+    dims 64, 128 and 256 (each a tensor-core attention instantiation).  hd 4096
+    marks the wide-MLP case (head dim 128, intermediate 4096): 700 tokens give
+    the persistent GEMM with the fused GeGLU epilogue."""
+    d = synth.tiny(window=16, head_dim=128, intermediate=4096) if hd == 4096 else synth.tiny(window=16, head_dim=hd)
     w = synth.make_weights(d, seed=21)
     d0 = d1 = None
     if head:

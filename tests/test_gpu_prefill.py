@@ -41,10 +41,15 @@ def _check(dims: synth.Gemma3Dims, prompt_len: int, *, mode: int = 0, seed: int 
     return {"logit_err": float(np.max(np.abs(dev - r))) / float(np.max(np.abs(r))), "kv_err": kv_err}
 
 
-@pytest.mark.parametrize(("prompt_len", "mode", "hd"), [(37, 0, 64), (130, 0, 64), (70, 1, 64), (300, 1, 64),
-                                                       (389, 0, 64), (260, 1, 256), (150, 0, 128)])
-def test_batched_prefill_matches_oracle(prompt_len: int, mode: int, hd: int) -> None:
-    res = _check(synth.tiny(window=32, head_dim=hd), prompt_len, mode=mode)
+@pytest.mark.parametrize(("prompt_len", "mode", "hd", "inter"), [(37, 0, 64, 512), (130, 0, 64, 512),
+                                                                (70, 1, 64, 512), (300, 1, 64, 512),
+                                                                (389, 0, 64, 512), (260, 1, 256, 512),
+                                                                (150, 0, 128, 512), (700, 1, 128, 4096)])
+def test_batched_prefill_matches_oracle(prompt_len: int, mode: int, hd: int, inter: int) -> None:
+    """The last case has enough 128 x 256 tiles (6 x 32) for the persistent GEMM
+    and its fused GeGLU epilogue; the others take the per-tile GEMM and the
+    separate GeGLU over interleaved gate / up columns."""
+    res = _check(synth.tiny(window=32, head_dim=hd, intermediate=inter), prompt_len, mode=mode)
     print(res)
     assert res["kv_err"] <= PF_TOL and res["logit_err"] <= PF_TOL, res
 
