@@ -210,13 +210,14 @@ def run_embed(args, world: int, rank: int, local: int) -> None:
     rng = np.random.default_rng(7)
     weights["embed_head.dense0.weight"] = (rng.standard_normal((EMBED_DENSE, d.hidden)) * 0.02).astype(np.float32)
     weights["embed_head.dense1.weight"] = (rng.standard_normal((d.hidden, EMBED_DENSE)) * 0.02).astype(np.float32)
-    lens = rng.integers(EMBED_LEN[0], EMBED_LEN[1] + 1, EMBED_BATCH)
+    nseq = args.embed_batch
+    lens = rng.integers(EMBED_LEN[0], EMBED_LEN[1] + 1, EMBED_BATCH)[:nseq]
     max_len = int(lens.max())
-    ids = np.zeros((EMBED_BATCH, max_len), np.int32)
+    ids = np.zeros((nseq, max_len), np.int32)
     for b, n in enumerate(lens):
         ids[b, :n] = synth.prompt_ids(int(n), d.vocab, seed=100 + b)
     lens32 = lens.astype(np.int32)
-    out = np.zeros((EMBED_BATCH, d.hidden), np.float32)
+    out = np.zeros((nseq, d.hidden), np.float32)
     rows = 64  # sequences per group (the model's max_batch)
     llm = _core.init_model(synth.metadata_of(weights), device=local, capacity=EMBED_LEN[1], max_batch=rows,
                            prefill_path=1, mode="gemma3", sliding_window=d.window)
@@ -225,7 +226,7 @@ def run_embed(args, world: int, rank: int, local: int) -> None:
 
     def step() -> None:
         _core._check(lib.mg_encode(h.ptr, ids.ctypes.data_as(_core._I32P), lens32.ctypes.data_as(_core._I32P),
-                                   EMBED_BATCH, max_len, out.ctypes.data_as(_core._F32P)))
+                                   nseq, max_len, out.ctypes.data_as(_core._F32P)))
 
     for _ in range(args.warmup):
         step()
@@ -270,19 +271,19 @@ def run_embed(args, world: int, rank: int, local: int) -> None:
     if rank == 0:
         print(json.dumps({
             "metric": "embedding encoder sequences/s (EmbeddingGemma-style 300M, 256 sequences, lengths U[16,512])",
-            "value": world * EMBED_BATCH / (ms / 1e3), "unit": "sequences/s", "n_gpus": world, "steps": args.steps,
+            "value": world * nseq / (ms / 1e3), "unit": "sequences/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16 (tcgen05, fp32 accumulate); attention and head fp32",
             "data": "synthetic (seeded N(0,0.02) random-init weights, uniform random ids and lengths)",
-            "config": {"workload": f"embedding-300m encoder, {EMBED_BATCH} sequences ({tokens} tokens), lengths "
+            "config": {"workload": f"embedding-300m encoder, {nseq} sequences ({tokens} tokens), lengths "
                                    f"U[{EMBED_LEN[0]},{EMBED_LEN[1]}], dense {d.hidden}->{EMBED_DENSE}->{d.hidden}, "
                                    f"groups of {rows} sequences", "model": "embedding-300m",
-                       "global_batch": world * EMBED_BATCH, "seq_len": EMBED_LEN[1],
+                       "global_batch": world * nseq, "seq_len": EMBED_LEN[1],
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "per-step activations and weights (>1.2 GB) larger than L2"},
-            "e2e": {"value": world * EMBED_BATCH / wall, "unit": "sequences/s",
-                    "h2d_bytes_per_step": 4 * (tokens * 4 + EMBED_BATCH * 2),
-                    "d2h_bytes_per_step": 4 * EMBED_BATCH * d.hidden},
+            "e2e": {"value": world * nseq / wall, "unit": "sequences/s",
+                    "h2d_bytes_per_step": 4 * (tokens * 4 + nseq * 2),
+                    "d2h_bytes_per_step": 4 * nseq * d.hidden},
             "roofline": {"bound": "tensor", "achieved": tf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": tf / pk["bf16_tflops"], "peak_source": pk["source"],
                          "kernel": "whole encoder step (projection GEMM FLOPs over the step time)",
@@ -290,7 +291,9 @@ def run_embed(args, world: int, rank: int, local: int) -> None:
                          "traffic": None},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
-            "gpu_launches": args.steps * (EMBED_BATCH // rows) * (2 + 9 * d.layers + 4),
+            # per group: embedding + first norm; per layer q/k/v GEMM, QK-norm/RoPE, V transpose, attention,
+            # o_proj GEMM, norm, gate/up GEMM (GeGLU fused), down GEMM, norm; head: 1/rms, pool, 2 dense, L2
+            "gpu_launches": args.steps * ((nseq + rows - 1) // rows) * (2 + 9 * d.layers + 5),
         }), flush=True)
     h.close()
     if world > 1:
@@ -392,6 +395,8 @@ def main() -> None:
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "embed"],
                     help="prefill: the batched tensor-core prefill of --prompt tokens; embed: the bidirectional "
                          "encoder on 256 sequences")
+    ap.add_argument("--embed-batch", type=int, default=EMBED_BATCH,
+                    help="embed: sequences per step (the workload is 256; fewer for small profiling captures)")
     ap.add_argument("--parallel", default="replicas", choices=["replicas", "tp"],
                     help="N>1: independent replicas (weak scaling) or one tensor-parallel model over the N GPUs")
     args = ap.parse_args()
