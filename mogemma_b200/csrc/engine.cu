@@ -35,7 +35,8 @@ cudaError_t sample_rows_launch(const float *logits, int64_t ld, int rows, int V,
 cudaError_t convert_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, void *dst, int dst_dtype,
                                 int64_t dst_ld, cudaStream_t stream);
 cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb, float *C, int64_t ldc, int M, int N,
-                         int K, uint32_t *err, cudaStream_t stream);
+                         int K, uint32_t *err, cudaStream_t stream, float *ws, size_t ws_floats);
+cudaError_t pf_advance(int32_t *pos, int n, cudaStream_t s);
 cudaError_t pf_embed(const void *E, int wdtype_bf16, int64_t ld, const int32_t *tok, int N, int H, float scale,
                      float *x, cudaStream_t s);
 cudaError_t pf_resnorm(const float *base, const float *add, const float *w_add, const float *w_next, float *res,
@@ -52,7 +53,7 @@ cudaError_t attn_tc(const __nv_bfloat16 *qb, const __nv_bfloat16 *kb, const __nv
 cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,
                          const float *vc, const int32_t *row, const int32_t *pos, const int32_t *last,
                          int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global, float scale,
-                         __nv_bfloat16 *out, int out_ld, cudaStream_t s);
+                         __nv_bfloat16 *out, int out_ld, int max_ctx, float *ws, size_t ws_floats, cudaStream_t s);
 cudaError_t pf_encoder_head(const float *x, int H, int N, const int32_t *start, const int32_t *len,
                             const float *final_norm, float inv_h, float *row_inv, const float *d0, int d0_out,
                             const float *d1, float *pool, float *mid, float *out, int B, cudaStream_t s);
@@ -169,6 +170,9 @@ struct mg_model {
     // tensor-core attention operands (bf16): Q [N][Hq*hd], K [N][Hkv*hd], V^T [Hkv*hd][pf_vt_ld]
     __nv_bfloat16 *pf_qb = nullptr, *pf_kb = nullptr, *pf_vt = nullptr;
     int64_t pf_vt_ld = 0;
+    float *pf_ws = nullptr;     // split-K partial products of small GEMM grids
+    size_t pf_ws_floats = 0;
+    int32_t *row_ident = nullptr;  // [nrows] = 0, 1, ...: the rows of a batched decode step
     int4 *att_tiles = nullptr;  // {start, len, q0, 0} per 128-query tile
     int att_tiles_cap = 0;
     // encoder head (embed_head.dense0 [d][H], embed_head.dense1 [H][d]; optional)
@@ -604,6 +608,15 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     TRY(upload_tiled(m, rows_view(*lmh, m->v0), m->V, m->H, 0, m->lm_head, wd, m->Hp, sh_h, 0, staging,
                      staging_bytes));
     m->weight_bytes += static_cast<int64_t>(we) * m->V * m->H;
+    if (m->prefill_path == 1 && m->tp == 1) {  // split-K workspace (8 MB) and the row identity
+        m->pf_ws_floats = static_cast<size_t>(2) << 20;
+        TRY(dalloc(m, &m->pf_ws, m->pf_ws_floats));
+        TRY(dalloc(m, &m->row_ident, m->nrows));
+        std::vector<int32_t> ident(m->nrows);
+        for (int b = 0; b < m->nrows; ++b) ident[b] = b;
+        CU(cudaMemcpyAsync(m->row_ident, ident.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice, m->stream));
+        CU(cudaStreamSynchronize(m->stream));
+    }
     if (m->Bmax > m->Bdec) {  // lm_head for batched decode steps
         TRY(dalloc(m, &m->pf_lm, static_cast<size_t>(m->V) * m->Hp));
         TRY(upload_matrix(m, *lmh, m->V, m->H, m->pf_lm, MG_BF16, m->Hp, staging, staging_bytes));
@@ -1133,7 +1146,9 @@ static int upload_att_tiles(mg_model *m, const std::vector<int32_t> &start, cons
 // position 0), and the attention runs on the tensor cores over those tiles;
 // last (encoder) selects the bidirectional mask.  Otherwise the CUDA-core
 // kernel reads the KV cache (prompts that continue a cached prefix).
-static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr, int ntiles = 0) {
+// max_ctx (> 0): an upper bound of the keys per token, which lets the
+// CUDA-core attention split the keys of a few tokens over many CTAs.
+static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr, int ntiles = 0, int max_ctx = 0) {
     cudaStream_t st = m->stream;
     const float inv_h = 1.0f / static_cast<float>(m->H), inv_hd = 1.0f / static_cast<float>(m->hd);
     const float att_scale = 1.0f / sqrtf(static_cast<float>(m->hd));
@@ -1142,7 +1157,7 @@ static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr, in
     CU(pf_resnorm(m->pf_x, nullptr, nullptr, m->h_layers[0].in_ln, m->pf_x, m->pf_xn, N, m->H, m->Hp, inv_h, st));
     auto gemm = [&](const __nv_bfloat16 *a, int lda, const __nv_bfloat16 *w, int n_out, int K, float *c,
                     int ldc) -> mg_status {
-        CU(gemm_bf16_tc(a, lda, w, K, c, ldc, N, n_out, K, m->err, st));
+        CU(gemm_bf16_tc(a, lda, w, K, c, ldc, N, n_out, K, m->err, st, m->pf_ws, m->pf_ws_floats));
         return MG_OK;
     };
     for (int l = 0; l < m->L; ++l) {
@@ -1167,7 +1182,7 @@ static mg_status pf_layers(mg_model *m, int N, const int32_t *last = nullptr, in
         else
             CU(pf_attention(m->pf_c, m->qkv_rows, N, m->Hq, m->Hkv, m->hd, m->hdp, kc, vc, m->pf_row, m->pf_pos,
                             last, m->kv_row_stride, m->kv_head_stride, m->window, lp.is_global, att_scale, m->pf_xn,
-                            m->Ap, st));
+                            m->Ap, max_ctx, m->pf_ws, m->pf_ws_floats, st));
         TRY(gemm(m->pf_xn, m->Ap, w.o, m->H, m->Ap, m->pf_c, m->H));
         CU(pf_resnorm(m->pf_x, m->pf_c, lp.post_attn_ln, lp.pre_ff_ln, m->pf_r, m->pf_xn, N, m->H, m->Hp, inv_h, st));
         // gate/up + GeGLU: fused into the GEMM epilogue when the grid fills the GPU
@@ -1226,19 +1241,19 @@ static mg_status step_batched(mg_model *m, int batch, const int32_t *tok_host, c
                               int32_t *out_tokens_dev) {
     TRY(pf_reserve(m, batch));
     cudaStream_t st = m->stream;
-    std::vector<int32_t> row(batch), pos(batch);
-    for (int b = 0; b < batch; ++b) {
-        row[b] = b;
-        pos[b] = m->h_pos[b];
-    }
+    // rows, positions and tokens come from device arrays (no pageable host
+    // copy, which could block the host): the step's launches queue ahead
     if (tok_host)
         CU(cudaMemcpyAsync(m->pf_tok, tok_host, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     else
         CU(cudaMemcpyAsync(m->pf_tok, m->tok, sizeof(int32_t) * batch, cudaMemcpyDeviceToDevice, st));
-    CU(cudaMemcpyAsync(m->pf_row, row.data(), sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
-    CU(cudaMemcpyAsync(m->pf_pos, pos.data(), sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
-    TRY(pf_layers(m, batch));
-    CU(gemm_bf16_tc(m->pf_xn, m->Hp, m->pf_lm, m->Hp, m->logits, m->V, batch, m->V, m->Hp, m->err, st));
+    CU(cudaMemcpyAsync(m->pf_row, m->row_ident, sizeof(int32_t) * batch, cudaMemcpyDeviceToDevice, st));
+    CU(cudaMemcpyAsync(m->pf_pos, m->pos, sizeof(int32_t) * batch, cudaMemcpyDeviceToDevice, st));
+    int max_ctx = 0;
+    for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, m->h_pos[b] + 1);
+    TRY(pf_layers(m, batch, nullptr, 0, max_ctx));
+    CU(gemm_bf16_tc(m->pf_xn, m->Hp, m->pf_lm, m->Hp, m->logits, m->V, batch, m->V, m->Hp, m->err, st, m->pf_ws,
+                    m->pf_ws_floats));
     if (s) {
         const double *u = nullptr;
         if (s->uniforms_host) {
@@ -1249,8 +1264,8 @@ static mg_status step_batched(mg_model *m, int batch, const int32_t *tok_host, c
                               m->rng_offset, out_tokens_dev, m->tok, st));
         m->rng_offset += 1;
     }
-    for (int b = 0; b < batch; ++b) m->h_pos[b] += 1;
-    CU(cudaMemcpyAsync(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice, st));
+    for (int b = 0; b < batch; ++b) m->h_pos[b] += 1;  // host mirror of the device increment
+    CU(pf_advance(m->pos, batch, st));
     return MG_OK;
 }
 

@@ -46,9 +46,11 @@ constexpr uint32_t kErrTcFull = 0x21000000u, kErrTcEmpty = 0x22000000u, kErrTcDo
 
 constexpr uint32_t kIdesc = idesc_bf16(kBM, kBN);
 
+// Split-K: blockIdx.z takes k steps [z nk_split, (z + 1) nk_split) and writes
+// its partial product to C + z c_split (a workspace the caller reduces).
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                        float *C, int M, int N, int K, int64_t ldc, uint32_t *err) {
+                        float *C, int M, int N, int K, int64_t ldc, int nk_split, int64_t c_split, uint32_t *err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[kStages], empty[kStages], done;
     __shared__ uint32_t tmem_slot;
@@ -57,7 +59,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t sb = sa + kStages * kABytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
-    const int nk = K / kBK;
+    const int kbeg = blockIdx.z * nk_split;
+    const int nk = min(nk_split, K / kBK - kbeg);  // k steps of this split (>= 1)
+    C += blockIdx.z * c_split;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -83,8 +87,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int s = kt % kStages;
             if (kt >= kStages && !mbar_wait(&empty[s], ((kt / kStages) - 1) & 1u, err, kErrTcEmpty)) break;
             mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
-            tma_load_2d(sa + s * kABytes, &map_a, kt * kBK, m0, smem_u32(&full[s]));
-            tma_load_2d(sb + s * kBBytes, &map_b, kt * kBK, n0, smem_u32(&full[s]));
+            tma_load_2d(sa + s * kABytes, &map_a, (kbeg + kt) * kBK, m0, smem_u32(&full[s]));
+            tma_load_2d(sb + s * kBBytes, &map_b, (kbeg + kt) * kBK, n0, smem_u32(&full[s]));
         }
     } else if (warp == 1 && lane == 0) {
         for (int kt = 0; kt < nk; ++kt) {
@@ -302,6 +306,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
 }  // namespace tc
 
 namespace tc {
+// C[m][n] = sum over the splits of ws[z][m][n] (ws rows N apart, splits M N apart)
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *ws, int splits, int M, int N, float *C,
+                                                           int64_t ldc) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    if (i >= static_cast<int64_t>(M) * N) return;
+    const int64_t m = i / N, n = i - m * N;
+    float acc = 0.f;
+    for (int z = 0; z < splits; ++z) acc += ws[static_cast<int64_t>(z) * M * N + i];
+    C[m * ldc + n] = acc;
+}
+
 static int g_sms = 0;  // SM count of the device, set with the kernels' shared-memory limits
 
 static cudaError_t gemm_setup() {
@@ -324,8 +339,12 @@ static cudaError_t gemm_setup() {
 
 // C[M][N] = A[M][K] . B[N][K]^T; A, B bf16 device memory (16-byte aligned rows),
 // K a multiple of 64, err a device word that receives a code on a timeout.
+// ws (optional, ws_floats long): workspace for split-K when the grid of
+// 128 x 128 tiles covers under half the SMs (few output columns, e.g. the
+// o_proj / down_proj of a batched decode step); the K steps are split so
+// the grid fills the GPU and a reduce kernel sums the partial products.
 cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb, float *C, int64_t ldc, int M, int N,
-                         int K, uint32_t *err, cudaStream_t stream) {
+                         int K, uint32_t *err, cudaStream_t stream, float *ws, size_t ws_floats) {
     using namespace tc;
     const cudaError_t e = gemm_setup();
     if (e != cudaSuccess) return e;
@@ -339,8 +358,26 @@ cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb,
         return cudaGetLastError();
     }
     if (!make_map_bf16(&ma, A, M, K, lda, kBM) || !make_map_bf16(&mb, B, N, K, ldb, kBN)) return cudaErrorInvalidValue;
+    const int nk = K / kBK;
+    const int tiles = ((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
+    int splits = 1;
+    if (ws && 2 * tiles < g_sms && nk >= 8) {
+        splits = std::min(std::min(nk / 4, 2 * g_sms / tiles), 32);  // >= 4 k steps per split
+        while (splits > 1 && static_cast<size_t>(splits) * M * N > ws_floats) --splits;
+    }
+    if (splits > 1) {
+        const int nk_split = (nk + splits - 1) / splits;
+        splits = (nk + nk_split - 1) / nk_split;  // every split non-empty
+        const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM, splits);
+        gemm_bf16_tc_kernel<<<grid, kThreads, kSmem, stream>>>(ma, mb, ws, M, N, K, N, nk_split,
+                                                               static_cast<int64_t>(M) * N, err);
+        const int64_t total = static_cast<int64_t>(M) * N;
+        splitk_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(ws, splits, M, N, C,
+                                                                                             ldc);
+        return cudaGetLastError();
+    }
     const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
-    gemm_bf16_tc_kernel<<<grid, kThreads, kSmem, stream>>>(ma, mb, C, M, N, K, ldc, err);
+    gemm_bf16_tc_kernel<<<grid, kThreads, kSmem, stream>>>(ma, mb, C, M, N, K, ldc, nk, 0, err);
     return cudaGetLastError();
 }
 
@@ -376,7 +413,7 @@ extern "C" mg_status mg_gemm_bf16(const void *a_dev, int64_t lda, const void *b_
         reinterpret_cast<uintptr_t>(a_dev) % 16 != 0 || reinterpret_cast<uintptr_t>(b_dev) % 16 != 0)
         return report_error(MG_ERR_INVALID, "mg_gemm_bf16: rows must be 16-byte aligned and strides >= extents");
     const cudaError_t e = gemm_bf16_tc(a_dev, lda, b_dev, ldb, c_dev, ldc, M, N, K, err_dev,
-                                       static_cast<cudaStream_t>(stream));
+                                       static_cast<cudaStream_t>(stream), nullptr, 0);
     if (e != cudaSuccess) {
         char buf[160];
         snprintf(buf, sizeof buf, "mg_gemm_bf16: %s", cudaGetErrorString(e));

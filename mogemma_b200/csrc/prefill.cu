@@ -18,6 +18,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "common.cuh"
@@ -118,6 +119,66 @@ __global__ void __launch_bounds__(kPfThreads) pf_resnorm_warp_kernel(const float
             const float4 x = r4[i], w = reinterpret_cast<const float4 *>(w_next)[i];
             y = make_float4(x.x * inv * (1.0f + w.x), x.y * inv * (1.0f + w.y), x.z * inv * (1.0f + w.z),
                             x.w * inv * (1.0f + w.w));
+        }
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(y.x, y.y), hi = __floats2bfloat162_rn(y.z, y.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t *>(&lo);
+        pk.y = *reinterpret_cast<const uint32_t *>(&hi);
+        reinterpret_cast<uint2 *>(xn + n * Kp)[i] = pk;
+    }
+}
+
+// The same for a few tokens (a batched decode step): one CTA per token, every
+// load of the row issued before the first reduction (H <= 4 kPfThreads float4s).
+__global__ void __launch_bounds__(kPfThreads) pf_resnorm_row_kernel(const float *base, const float *add,
+                                                                    const float *w_add, const float *w_next,
+                                                                    float *res, __nv_bfloat16 *xn, int H, int Kp,
+                                                                    float inv_h) {
+    constexpr int kJ = 4;
+    __shared__ float red[kPfThreads / 32];
+    const int64_t n = blockIdx.x;
+    const int H4 = H / 4;
+    const float4 *b4 = reinterpret_cast<const float4 *>(base + n * H);
+    const float4 *a4 = add ? reinterpret_cast<const float4 *>(add + n * H) : nullptr;
+    float4 x[kJ], a[kJ], wa[kJ], wn[kJ];
+#pragma unroll
+    for (int j = 0; j < kJ; ++j) {
+        const int i = threadIdx.x + j * kPfThreads;
+        const bool on = i < H4;
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        x[j] = on ? b4[i] : z;
+        a[j] = (on && add) ? a4[i] : z;
+        wa[j] = (on && add) ? reinterpret_cast<const float4 *>(w_add)[i] : z;
+        wn[j] = on ? reinterpret_cast<const float4 *>(w_next)[i] : z;
+    }
+    if (add) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) s += a[j].x * a[j].x + a[j].y * a[j].y + a[j].z * a[j].z + a[j].w * a[j].w;
+        const float inv_a = rms_inv(block_sum_pf(s, red), inv_h);
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) {
+            x[j].x += a[j].x * inv_a * (1.0f + wa[j].x);
+            x[j].y += a[j].y * inv_a * (1.0f + wa[j].y);
+            x[j].z += a[j].z * inv_a * (1.0f + wa[j].z);
+            x[j].w += a[j].w * inv_a * (1.0f + wa[j].w);
+        }
+    }
+    float s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < kJ; ++j) {
+        const int i = threadIdx.x + j * kPfThreads;
+        if (i < H4) reinterpret_cast<float4 *>(res + n * H)[i] = x[j];
+        s2 += x[j].x * x[j].x + x[j].y * x[j].y + x[j].z * x[j].z + x[j].w * x[j].w;
+    }
+    const float inv = rms_inv(block_sum_pf(s2, red), inv_h);
+    for (int i = threadIdx.x; i < Kp / 4; i += kPfThreads) {
+        float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) {
+            if (i == static_cast<int>(threadIdx.x) + j * kPfThreads && i < H4)
+                y = make_float4(x[j].x * inv * (1.0f + wn[j].x), x[j].y * inv * (1.0f + wn[j].y),
+                                x[j].z * inv * (1.0f + wn[j].z), x[j].w * inv * (1.0f + wn[j].w));
         }
         const __nv_bfloat162 lo = __floats2bfloat162_rn(y.x, y.y), hi = __floats2bfloat162_rn(y.z, y.w);
         uint2 pk;
@@ -276,11 +337,14 @@ __global__ void __launch_bounds__(kPfThreads) pf_v_transpose_kernel(const float 
 // read as a broadcast), a warp-wide max/sum per head updates that warp's
 // online softmax, and P.V runs with lanes over head dims.  The warps' partial
 // (m, l, acc) are combined in shared memory.
+// Split-KV (kchunk > 0, few tokens such as a batched decode step): blockIdx.y
+// takes keys [lo + y kchunk, lo + (y + 1) kchunk) and the CTA writes its
+// (m, l, unnormalised acc) per q head to part; pf_attn_combine_kernel merges.
 template <int GQ>
 __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
     const float *qkv, int qkv_ld, int Hq, int Hkv, int hd, int hdp, const float *kc, const float *vc,
     const int32_t *row, const int32_t *pos, const int32_t *last, int64_t kv_row_stride, int64_t kv_head_stride,
-    int window, int is_global, float scale, __nv_bfloat16 *out, int out_ld, int N) {
+    int window, int is_global, float scale, __nv_bfloat16 *out, int out_ld, int N, int kchunk, float *part) {
     constexpr int kQ = GQ > 0 ? GQ : kMaxQPerKv;
     constexpr int kDL = kMaxHeadDim / 32;
     constexpr int kW = kPfThreads / 32;
@@ -315,7 +379,12 @@ __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
 #pragma unroll
         for (int i = 0; i < kDL; ++i) acc[h][i] = 0.f;
     }
-    for (int t0 = lo + 32 * w; t0 <= hi; t0 += 32 * kW) {
+    int klo = lo, khi = hi;
+    if (kchunk > 0) {
+        klo = lo + static_cast<int>(blockIdx.y) * kchunk;
+        khi = min(hi, klo + kchunk - 1);
+    }
+    for (int t0 = klo + 32 * w; t0 <= khi; t0 += 32 * kW) {
         const int t = t0 + lane;
         const bool valid = t <= hi;
         float s[kQ];
@@ -396,6 +465,37 @@ __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
             const float f = expf(mu - M);
             L += pl[u * gq + h] * f;
             o += pacc[(u * gq + h) * hd + d] * f;
+        }
+        if (part) {  // [N * Hkv][splits][gq][2 + hd]: m, l, acc
+            float *pp = part + ((static_cast<int64_t>(blockIdx.x) * gridDim.y + blockIdx.y) * gq + h) * (hd + 2);
+            if (d == 0) {
+                pp[0] = M;
+                pp[1] = L;
+            }
+            pp[2 + d] = M == -INFINITY ? 0.f : o;
+        } else {
+            out[n * out_ld + static_cast<int64_t>(kvh * gq + h) * hd + d] = __float2bfloat16_rn(o / L);
+        }
+    }
+}
+
+// out[n][(kvh gq + h) hd + d] from the splits' (m, l, acc) of (token n, kv head kvh).
+__global__ void __launch_bounds__(kPfThreads) pf_attn_combine_kernel(const float *part, int splits, int gq, int hd,
+                                                                     int Hkv, __nv_bfloat16 *out, int out_ld) {
+    const int64_t n = blockIdx.x / Hkv;
+    const int kvh = static_cast<int>(blockIdx.x - n * Hkv);
+    const float *base = part + static_cast<int64_t>(blockIdx.x) * splits * gq * (hd + 2);
+    for (int e = threadIdx.x; e < gq * hd; e += kPfThreads) {
+        const int h = e / hd, d = e - h * hd;
+        float M = -INFINITY;
+        for (int y = 0; y < splits; ++y) M = fmaxf(M, base[(y * gq + h) * (hd + 2)]);
+        float L = 0.f, o = 0.f;
+        for (int y = 0; y < splits; ++y) {
+            const float *pp = base + (y * gq + h) * (hd + 2);
+            if (pp[0] == -INFINITY) continue;  // a split with no key in range
+            const float f = expf(pp[0] - M);
+            L += pp[1] * f;
+            o += pp[2 + d] * f;
         }
         out[n * out_ld + static_cast<int64_t>(kvh * gq + h) * hd + d] = __float2bfloat16_rn(o / L);
     }
@@ -521,7 +621,9 @@ cudaError_t pf_embed(const void *E, int wdtype_bf16, int64_t ld, const int32_t *
 }
 cudaError_t pf_resnorm(const float *base, const float *add, const float *w_add, const float *w_next, float *res,
                        __nv_bfloat16 *xn, int N, int H, int Kp, float inv_h, cudaStream_t s) {
-    if (H % 4 == 0 && Kp % 4 == 0)
+    if (H % 4 == 0 && Kp % 4 == 0 && N < 8 * 148 && H <= 16 * kPfThreads)
+        pf_resnorm_row_kernel<<<N, kPfThreads, 0, s>>>(base, add, w_add, w_next, res, xn, H, Kp, inv_h);
+    else if (H % 4 == 0 && Kp % 4 == 0)
         pf_resnorm_warp_kernel<<<(N + kPfThreads / 32 - 1) / (kPfThreads / 32), kPfThreads, 0, s>>>(
             base, add, w_add, w_next, res, xn, H, Kp, inv_h, N);
     else
@@ -565,8 +667,20 @@ cudaError_t pf_qk_rope_kv(float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd
 cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, int hd, int hdp, const float *kc,
                          const float *vc, const int32_t *row, const int32_t *pos, const int32_t *last,
                          int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global, float scale,
-                         __nv_bfloat16 *out, int out_ld, cudaStream_t s) {
+                         __nv_bfloat16 *out, int out_ld, int max_ctx, float *ws, size_t ws_floats, cudaStream_t s) {
     const int blocks = N * Hkv;
+    // few (token, kv head) pairs and long contexts: split the keys so the grid
+    // covers about two waves of SMs (blocks of 64+ keys), then merge
+    int splits = 1, kchunk = 0;
+    if (ws && blocks < 148 && max_ctx > 128) {
+        splits = std::min((max_ctx + 63) / 64, std::max(1, 2 * 148 / blocks));
+        kchunk = (max_ctx + splits - 1) / splits;
+        kchunk = (kchunk + 31) / 32 * 32;
+        splits = (max_ctx + kchunk - 1) / kchunk;
+        if (static_cast<size_t>(blocks) * splits * (Hq / Hkv) * (hd + 2) > ws_floats) splits = 1, kchunk = 0;
+    }
+    float *part = splits > 1 ? ws : nullptr;
+    if (splits == 1) kchunk = 0;
     const int gq = Hq / Hkv;
     const size_t smem = sizeof(float) * (static_cast<size_t>(gq) * hd * (1 + kPfThreads / 32) + 2 * (kPfThreads / 32) * gq);
 #define MG_PF_ATT(G)                                                                                                \
@@ -577,9 +691,9 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
                                                        static_cast<int>(smem));                                     \
             if (e != cudaSuccess) return e;                                                                         \
         }                                                                                                           \
-        pf_attention_kernel<G><<<blocks, kPfThreads, smem, s>>>(qkv, qkv_ld, Hq, Hkv, hd, hdp, kc, vc, row, pos,   \
-                                                                last, kv_row_stride, kv_head_stride, window,        \
-                                                                is_global, scale, out, out_ld, N);                  \
+        pf_attention_kernel<G><<<dim3(blocks, splits), kPfThreads, smem, s>>>(                                      \
+            qkv, qkv_ld, Hq, Hkv, hd, hdp, kc, vc, row, pos, last, kv_row_stride, kv_head_stride, window, is_global,  \
+            scale, out, out_ld, N, kchunk, part);                                                                   \
     } while (0)
     switch (Hq / Hkv) {
         case 1: MG_PF_ATT(1); break;
@@ -588,6 +702,17 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
         default: MG_PF_ATT(0); break;
     }
 #undef MG_PF_ATT
+    if (part)
+        pf_attn_combine_kernel<<<blocks, kPfThreads, 0, s>>>(part, splits, Hq / Hkv, hd, Hkv, out, out_ld);
+    return cudaGetLastError();
+}
+// pos[b] += 1 for rows [0, n): the positions after a batched decode step.
+__global__ void pf_advance_kernel(int32_t *pos, int n) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < n) pos[b] += 1;
+}
+cudaError_t pf_advance(int32_t *pos, int n, cudaStream_t s) {
+    pf_advance_kernel<<<(n + 127) / 128, 128, 0, s>>>(pos, n);
     return cudaGetLastError();
 }
 cudaError_t pf_geglu(const float *gu, int I, int gu_ld, __nv_bfloat16 *act, int Ip, int N, int il, cudaStream_t s) {
