@@ -479,6 +479,147 @@ __global__ void __launch_bounds__(kPfThreads) pf_attention_kernel(
     }
 }
 
+// Decode-shaped split of the attention (one query per (token, kv head), a key
+// range per blockIdx.y, as pf_attention_kernel with kchunk > 0): lanes run over
+// head dims, so every key row is one coalesced warp load; each warp takes keys
+// four at a time (interleaved with the other warps) and keeps its own online
+// softmax per q head; the 8 warps merge in shared memory and the CTA writes
+// its split's (m, l, unnormalised acc) to part for pf_attn_combine_kernel.
+template <int GQ, int HD>
+__global__ void __launch_bounds__(kPfThreads) pf_attn_decode_kernel(
+    const float *qkv, int qkv_ld, int Hkv, int hdp, const float *kc, const float *vc, const int32_t *row,
+    const int32_t *pos, int64_t kv_row_stride, int64_t kv_head_stride, int window, int is_global, float scale,
+    int kchunk, float *part) {
+    constexpr int kW = kPfThreads / 32;
+    constexpr int kJ = (HD + 127) / 128;  // float4 of a head row per lane
+    constexpr int kB = 4;                 // keys per warp step
+    __shared__ float sm_m[kW][GQ], sm_l[kW][GQ];
+    __shared__ __align__(16) float sm_acc[kW][GQ][HD];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t n = blockIdx.x / Hkv;
+    const int kvh = static_cast<int>(blockIdx.x - n * Hkv);
+    const int p = pos[n];
+    const int lo = (!is_global && window > 0 && p - window + 1 > 0) ? p - window + 1 : 0;
+    const int klo = lo + static_cast<int>(blockIdx.y) * kchunk;
+    const int khi = min(p, klo + kchunk - 1);
+    const float *qb = qkv + n * qkv_ld + static_cast<int64_t>(kvh) * GQ * HD;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 q[GQ][kJ];
+#pragma unroll
+    for (int h = 0; h < GQ; ++h)
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) {
+            const int f = lane + 32 * j;
+            q[h][j] = 4 * f < HD ? *reinterpret_cast<const float4 *>(qb + h * HD + 4 * f) : z4;
+        }
+    const int64_t kvoff = row[n] * kv_row_stride + kvh * kv_head_stride;
+    const float *kb = kc + kvoff, *vb = vc + kvoff;
+    float m[GQ], l[GQ];
+    float4 acc[GQ][kJ];
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) acc[h][j] = z4;
+    }
+    for (int t0 = klo + w * kB; t0 <= khi; t0 += kW * kB) {
+        float4 kr[kB][kJ], vr[kB][kJ];
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+            const int t = t0 + b;
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) {
+                const int f = lane + 32 * j;
+                const bool on = t <= khi && 4 * f < HD;
+                kr[b][j] = on ? *reinterpret_cast<const float4 *>(kb + static_cast<int64_t>(t) * hdp + 4 * f) : z4;
+                vr[b][j] = on ? *reinterpret_cast<const float4 *>(vb + static_cast<int64_t>(t) * hdp + 4 * f) : z4;
+            }
+        }
+        float sc[kB][GQ];
+#pragma unroll
+        for (int b = 0; b < kB; ++b)
+#pragma unroll
+            for (int h = 0; h < GQ; ++h) {
+                float a = 0.f;
+#pragma unroll
+                for (int j = 0; j < kJ; ++j)
+                    a += q[h][j].x * kr[b][j].x + q[h][j].y * kr[b][j].y + q[h][j].z * kr[b][j].z +
+                         q[h][j].w * kr[b][j].w;
+                sc[b][h] = a;
+            }
+#pragma unroll
+        for (int b = 0; b < kB; ++b)
+#pragma unroll
+            for (int h = 0; h < GQ; ++h) sc[b][h] = t0 + b <= khi ? warp_sum(sc[b][h]) * scale : -INFINITY;
+#pragma unroll
+        for (int h = 0; h < GQ; ++h) {
+            float mx = sc[0][h];
+#pragma unroll
+            for (int b = 1; b < kB; ++b) mx = fmaxf(mx, sc[b][h]);
+            const float m_new = fmaxf(m[h], mx);
+            const float alpha = m[h] == -INFINITY ? 0.f : expf(m[h] - m_new);
+            float pb[kB], ps = 0.f;
+#pragma unroll
+            for (int b = 0; b < kB; ++b) {
+                pb[b] = sc[b][h] == -INFINITY ? 0.f : expf(sc[b][h] - m_new);
+                ps += pb[b];
+            }
+            l[h] = l[h] * alpha + ps;
+            m[h] = m_new;
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) {
+                float4 a = acc[h][j];
+                a.x *= alpha;
+                a.y *= alpha;
+                a.z *= alpha;
+                a.w *= alpha;
+#pragma unroll
+                for (int b = 0; b < kB; ++b) {
+                    a.x += pb[b] * vr[b][j].x;
+                    a.y += pb[b] * vr[b][j].y;
+                    a.z += pb[b] * vr[b][j].z;
+                    a.w += pb[b] * vr[b][j].w;
+                }
+                acc[h][j] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+        if (lane == 0) {
+            sm_m[w][h] = m[h];
+            sm_l[w][h] = l[h];
+        }
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) {
+            const int f = lane + 32 * j;
+            if (4 * f < HD) *reinterpret_cast<float4 *>(&sm_acc[w][h][4 * f]) = acc[h][j];
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < GQ * HD; e += kPfThreads) {
+        const int h = e / HD, d = e - h * HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < kW; ++u) M = fmaxf(M, sm_m[u][h]);
+        float L = 0.f, o = 0.f;
+#pragma unroll
+        for (int u = 0; u < kW; ++u) {
+            if (sm_m[u][h] == -INFINITY) continue;  // a warp that saw no key
+            const float f = expf(sm_m[u][h] - M);
+            L += sm_l[u][h] * f;
+            o += sm_acc[u][h][d] * f;
+        }
+        float *pp = part + ((static_cast<int64_t>(blockIdx.x) * gridDim.y + blockIdx.y) * GQ + h) * (HD + 2);
+        if (d == 0) {
+            pp[0] = M;
+            pp[1] = L;
+        }
+        pp[2 + d] = M == -INFINITY ? 0.f : o;
+    }
+}
+
 // out[n][(kvh gq + h) hd + d] from the splits' (m, l, acc) of (token n, kv head kvh).
 __global__ void __launch_bounds__(kPfThreads) pf_attn_combine_kernel(const float *part, int splits, int gq, int hd,
                                                                      int Hkv, __nv_bfloat16 *out, int out_ld) {
@@ -695,11 +836,27 @@ cudaError_t pf_attention(const float *qkv, int qkv_ld, int N, int Hq, int Hkv, i
             qkv, qkv_ld, Hq, Hkv, hd, hdp, kc, vc, row, pos, last, kv_row_stride, kv_head_stride, window, is_global,  \
             scale, out, out_ld, N, kchunk, part);                                                                   \
     } while (0)
-    switch (Hq / Hkv) {
-        case 1: MG_PF_ATT(1); break;
-        case 2: MG_PF_ATT(2); break;
-        case 4: MG_PF_ATT(4); break;
-        default: MG_PF_ATT(0); break;
+    bool done = false;
+    if (part) {  // decode-shaped split: coalesced key rows
+#define MG_PF_DEC(G, HD_)                                                                                           \
+    if (gq == G && hd == HD_) {                                                                                     \
+        pf_attn_decode_kernel<G, HD_><<<dim3(blocks, splits), kPfThreads, 0, s>>>(                                  \
+            qkv, qkv_ld, Hkv, hdp, kc, vc, row, pos, kv_row_stride, kv_head_stride, window, is_global, scale, kchunk, \
+            part);                                                                                                  \
+        done = true;                                                                                                \
+    }
+        MG_PF_DEC(1, 256) MG_PF_DEC(2, 256) MG_PF_DEC(3, 256) MG_PF_DEC(4, 256)
+        MG_PF_DEC(1, 128) MG_PF_DEC(2, 128) MG_PF_DEC(4, 128)
+        MG_PF_DEC(1, 64) MG_PF_DEC(2, 64) MG_PF_DEC(4, 64)
+#undef MG_PF_DEC
+    }
+    if (!done) {
+        switch (Hq / Hkv) {
+            case 1: MG_PF_ATT(1); break;
+            case 2: MG_PF_ATT(2); break;
+            case 4: MG_PF_ATT(4); break;
+            default: MG_PF_ATT(0); break;
+        }
     }
 #undef MG_PF_ATT
     if (part)

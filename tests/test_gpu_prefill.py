@@ -115,3 +115,22 @@ def test_batched_decode_rows_beyond_persistent_kernel() -> None:
     _core._check(_core.lib().mg_generate(h.ptr, 4, rows, _core.ctypes.byref(s), out.ctypes.data_as(_core._I32P)))
     assert h.get_pos()[:rows] == [p + 4 for p in before]
     assert ((out >= 0) & (out < d.vocab)).all()
+
+
+@pytest.mark.parametrize("hd", [128, 256])
+def test_batched_decode_long_context_split_attention(hd: int) -> None:
+    """12 rows with 140-283 cached positions: the batched step splits each
+    row's keys over several CTAs (decode-shaped split attention + merge)."""
+    d = synth.tiny(head_dim=hd)
+    w = synth.make_weights(d, seed=31)
+    rows = 12
+    prompts = [[int(t) for t in synth.prompt_ids(141 + 13 * i, d.vocab, seed=70 + i)] for i in range(rows)]
+    llm = _core.init_model(synth.metadata_of(w), prefill_path=1, max_batch=rows, capacity=320)
+    _core.prefill_rows(llm, [p[:-1] for p in prompts])
+    logits, _ = _core.step_rows(llm, [p[-1] for p in prompts], sampling=(0.0, 0, 1.0))
+    for b, pr in enumerate(prompts):
+        ref = oracle.RefModel(w, max_seq_len=320)
+        for t in pr[:-1]:
+            ref.step_no_logits(t)
+        r = ref.step(pr[-1])
+        assert float(np.max(np.abs(logits[b] - r))) <= PF_TOL * float(np.max(np.abs(r))), b
