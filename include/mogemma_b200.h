@@ -198,8 +198,9 @@ mg_status mg_read_kv(const mg_model *m, int32_t layer, int32_t row, int32_t pos,
 /* ---- timeline (profiling; no reference counterpart: the reference only has
  * OpenTelemetry spans around whole calls, src/py/mogemma/telemetry.py) ----
  * When enabled, every decode launch records %globaltimer stamps per CTA and
- * phase: [ctas][phases][6] (start, ready, first tile, end, producer start,
- * producer end) followed by [ctas][2] kernel begin/end.  mg_trace_read copies
+ * phase: [ctas][phases][10] (start, ready, first tile, end, producer start,
+ * producer end, then for attention phases: q/k/v loaded, normed and rotated,
+ * tiles done, partial written) followed by [ctas][2] kernel begin/end.  mg_trace_read copies
  * the stamps of the most recent launch; *n_out receives the element count. */
 mg_status mg_trace_enable(mg_model *m, int32_t on);
 mg_status mg_trace_read(mg_model *m, uint64_t *out_host, int64_t capacity, int64_t *n_out);
