@@ -497,7 +497,8 @@ def main() -> None:
         cpu = cpu_baseline(weights, 1, args.cpu_sample)
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if B == 1 else METRIC.replace("batch-1", f"batch-{B}"), "value": value, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": args.weight_dtype,
