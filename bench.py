@@ -116,8 +116,8 @@ def algorithmic_bytes(info, pos0: int, n: int, rows: int = 1) -> float:
 
 # DRAM bytes (read + write) per decode launch over its algorithmic bytes, from
 # one ncu capture of this kernel on the Gemma3-270M shape (the full Gemma3-1B
-# workload is too large to capture): profiles/decode_kernel_gemma3-270m_full.md.
-# Traffic is almost all weight reads, so it scales with the algorithmic bytes.
+# workload is too large to capture).  Traffic is almost all weight reads, so
+# it scales with the algorithmic bytes.
 TRAFFIC_RATIO = {("gemma3-1b", "f32"): 1.0036, ("gemma3-270m", "f32"): 1.0036}
 
 

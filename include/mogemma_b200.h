@@ -163,9 +163,10 @@ mg_status mg_sample(const float *logits_host, int32_t batch, int32_t vocab, cons
  * 0 < top_k <= 64 (MG_ERR_INVALID / MG_ERR_UNSUPPORTED beyond).  Its only
  * scratch is a static device array of 8 * 148 * 64 candidate keys (606,208
  * bytes) shared by every call on a device: calls that overlap on the GPU race;
- * calls on one stream are safe.  The first call on a device (the current one)
- * resolves the array's address and a kernel attribute; make it before any
- * stream capture. */
+ * calls on one stream are safe.  Every call resolves the array's address and
+ * a kernel attribute on the current device (nothing is cached, so a context
+ * recreated by cudaDeviceReset is picked up); the first call on a device loads
+ * the kernels there: make it before any stream capture. */
 #define MG_SAMPLE_STATIC_MAX_ROWS 8
 #define MG_SAMPLE_STATIC_MAX_SLICES 148
 mg_status mg_sample_static(const float *logits_dev, int64_t ld, int32_t batch, int32_t vocab, double temperature,

@@ -18,10 +18,13 @@
 // below.  Greedy (temperature <= 0) and 0 < top_k <= 64 are covered (top_p on
 // top of either); the result equals mg_sample's token for token.
 //
-// Set-up: the first call on a device (the device current on the calling host
-// thread) looks up the array's device address with cudaGetSymbolAddress and
-// raises the merge kernel's dynamic shared-memory limit; later calls reuse
-// both.  Make that first call before any stream capture.
+// Set-up: every call, with the calling thread's current device, looks up the
+// array's device address with cudaGetSymbolAddress and raises the merge
+// kernel's dynamic shared-memory limit (host-side table lookups, no
+// allocation).  Nothing is cached across calls, so a context that the caller
+// tears down and recreates (cudaDeviceReset) gets the new module's address.
+// The first call on a device loads the library's kernels onto it; make that
+// first call before any stream capture.
 //
 // Sharing: every call on a device uses the same array.  Two calls whose
 // kernels overlap on the GPU (different streams, no ordering between them)
@@ -33,7 +36,6 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstdio>
-#include <mutex>
 
 #include "../../include/mogemma_b200.h"
 #include "common.cuh"
@@ -49,7 +51,6 @@ constexpr int kStMaxSlices = MG_SAMPLE_STATIC_MAX_SLICES;
 constexpr int kStSliceMin = 1024;  // vocabulary entries per slice before another slice is opened
 constexpr size_t kStKeys = static_cast<size_t>(kStMaxRows) * kStMaxSlices * kMaxTopK;
 constexpr size_t kStMergeSmem = static_cast<size_t>(kStMaxSlices) * kMaxTopK * sizeof(uint64_t);
-constexpr int kStMaxDevices = 64;
 
 // Candidate keys [row][slice][K] of the current call: 8 * 148 * 64 * 8 bytes = 606,208 bytes.
 static __device__ __align__(256) uint64_t g_st_cand[kStKeys];
@@ -94,35 +95,22 @@ __global__ void __launch_bounds__(kStThreads)
 }
 
 namespace {
-struct StSetup {
-    bool done = false;
-    uint64_t *cand = nullptr;
-};
-std::mutex g_st_mu;
-StSetup g_st[kStMaxDevices];
-
 mg_status st_error(mg_status st, const char *what, cudaError_t e) {
     char buf[256];
     snprintf(buf, sizeof buf, "mg_sample_static: %s failed: %s", what, cudaGetErrorString(e));
     return report_error(st, buf);
 }
 
-// Once per device, with that device current.
-mg_status st_setup(int dev, uint64_t **cand) {
-    std::lock_guard<std::mutex> lock(g_st_mu);
-    if (dev < 0 || dev >= kStMaxDevices) return report_error(MG_ERR_UNSUPPORTED, "mg_sample_static: device ordinal out of range");
-    StSetup &s = g_st[dev];
-    if (!s.done) {
-        void *ptr = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&ptr, g_st_cand);
-        if (e != cudaSuccess) return st_error(MG_ERR_CUDA, "cudaGetSymbolAddress", e);
-        e = cudaFuncSetAttribute(st_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kStMergeSmem));
-        if (e != cudaSuccess) return st_error(MG_ERR_CUDA, "cudaFuncSetAttribute", e);
-        s.cand = static_cast<uint64_t *>(ptr);
-        s.done = true;
-    }
-    *cand = s.cand;
+// The array's address on the current device, and the merge kernel's shared
+// memory limit; repeated on every call (see the header comment).
+mg_status st_setup(uint64_t **cand) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_st_cand);
+    if (e != cudaSuccess) return st_error(MG_ERR_CUDA, "cudaGetSymbolAddress", e);
+    e = cudaFuncSetAttribute(st_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kStMergeSmem));
+    if (e != cudaSuccess) return st_error(MG_ERR_CUDA, "cudaFuncSetAttribute", e);
+    *cand = static_cast<uint64_t *>(ptr);
     return MG_OK;
 }
 }  // namespace
@@ -150,16 +138,13 @@ extern "C" mg_status mg_sample_static(const float *logits_dev, int64_t ld, int32
                  kMaxTopK, kMaxTopK);
         return report_error(MG_ERR_UNSUPPORTED, buf);
     }
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return st_error(MG_ERR_CUDA, "cudaGetDevice", e);
     uint64_t *cand = nullptr;
-    mg_status st = st_setup(dev, &cand);
+    mg_status st = st_setup(&cand);
     if (st != MG_OK) return st;
     const int slices = std::min(kStMaxSlices, (vocab + kStSliceMin - 1) / kStSliceMin);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     st_slice_topk_kernel<<<dim3(slices, batch), kStThreads, 0, s>>>(logits_dev, ld, vocab, slices, K, cand);
-    e = cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return st_error(MG_ERR_CUDA, "slice top-k launch", e);
     const size_t smem = static_cast<size_t>(slices) * K * sizeof(uint64_t);
     st_draw_kernel<<<batch, kStThreads, smem, s>>>(cand, slices, K, temperature, top_p, uniforms_dev, seed, offset,

@@ -18,18 +18,42 @@ from __future__ import annotations
 
 import asyncio
 import contextlib
-from collections.abc import AsyncIterator, Generator, Sequence
+from collections.abc import AsyncIterator, Generator, Iterator, Sequence
 from pathlib import Path
 from typing import Any, Protocol, cast
 
 import numpy as np
 import numpy.typing as npt
 
-from ._typing import SENTENCEPIECE_INSTALLED, _SPProcessorImpl
 from .config import EmbeddingConfig, GenerationConfig
 from .hub import HubManager
 from .loader import ModelLoader, auto_loader
-from .telemetry import tracer
+
+# Optional dependencies.  The names are module globals so that callers (and
+# tests) can switch tokenization off the way the reference package allows.
+try:
+    from sentencepiece import SentencePieceProcessor as _SentencePiece  # type: ignore[import-untyped]
+except ModuleNotFoundError:
+    _SentencePiece = None
+SENTENCEPIECE_INSTALLED = _SentencePiece is not None
+
+try:
+    from opentelemetry import trace as _otel
+except ModuleNotFoundError:
+    _otel = None
+
+
+@contextlib.contextmanager
+def _span(name: str, **attributes: object) -> Iterator[None]:
+    """An OpenTelemetry span named ``name`` carrying ``attributes`` when the
+    package is installed; otherwise nothing is recorded."""
+    if _otel is None:
+        yield
+        return
+    with _otel.get_tracer("mogemma_b200").start_as_current_span(name) as span:
+        for key, value in attributes.items():
+            span.set_attribute(key, value)
+        yield
 
 try:
     from . import _core
@@ -47,9 +71,9 @@ class _Tokenizer:
     """sentencepiece wrapper with the small surface the models use."""
 
     def __init__(self, model_path: str) -> None:
-        if _SPProcessorImpl is None:
+        if _SentencePiece is None:
             raise ModuleNotFoundError("sentencepiece runtime is unavailable")
-        self.sp = _SPProcessorImpl(model_file=model_path)
+        self.sp = _SentencePiece(model_file=model_path)
         self._max_length: int | None = None
 
     def enable_truncation(self, *, max_length: int, **_: object) -> None:
@@ -194,16 +218,15 @@ class EmbeddingModel:
 
     def embed(self, text: str | list[str]) -> npt.NDArray[np.float32]:
         """Tokenize ``text`` and return one embedding row per input."""
-        with tracer.start_as_current_span("EmbeddingModel.embed") as span:
-            texts = [text] if isinstance(text, str) else text
-            if not texts:
-                raise ValueError("text input must contain at least one value")
-            span.set_attribute("text_count", len(texts))
+        texts = [text] if isinstance(text, str) else text
+        if not texts:
+            raise ValueError("text input must contain at least one value")
         tokenizer = self._ensure_tokenizer()
-        tokenizer.enable_truncation(max_length=self.config.max_sequence_length)
-        tokenizer.enable_padding()
-        tokens = [e.ids for e in tokenizer.encode_batch(texts)]
-        return self._embed_token_array(tokens, len(texts))
+        with _span("EmbeddingModel.embed", text_count=len(texts)):
+            tokenizer.enable_truncation(max_length=self.config.max_sequence_length)
+            tokenizer.enable_padding()
+            tokens = [e.ids for e in tokenizer.encode_batch(texts)]
+            return self._embed_token_array(tokens, len(texts))
 
     def embed_tokens(self, tokens: Sequence[Sequence[int]] | npt.NDArray[np.int32]) -> npt.NDArray[np.float32]:
         """Embed pre-tokenized id rows."""
@@ -257,8 +280,7 @@ class SyncGemmaModel:
 
     def _prompt_tokens(self, tokenizer: _Tokenizer, prompt: str) -> list[int]:
         text = _format_instruction_prompt(prompt) if self._instruction_tuned else prompt
-        with tracer.start_as_current_span("SyncGemmaModel.generate_stream") as span:
-            span.set_attribute("prompt_length", len(prompt))
+        with _span("SyncGemmaModel.generate_stream", prompt_length=len(prompt)):
             tokenizer.enable_truncation(max_length=self.config.max_sequence_length)
             tokenizer.enable_padding()
             tokens = list(tokenizer.encode(text).ids)

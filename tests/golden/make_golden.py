@@ -1,7 +1,8 @@
 """Generate tests/golden/*.json from the reference's own Python code.
 
-Run in a container where the reference is mounted (read-only) at
-/root/reference:  python tests/golden/make_golden.py
+Run where a checkout of the reference is readable:
+  python tests/golden/make_golden.py REFERENCE_DIR
+(REFERENCE_DIR: the reference project's root, holding src/py and src/mo).
 
 * sampling.json: outputs of the reference ``_sample_next_token``
   (src/py/mogemma/model.py:103-150) on seeded logits.  The reference draws with
@@ -12,7 +13,7 @@ Run in a container where the reference is mounted (read-only) at
   layer tests (src/mo/tests/test_ops.mojo, src/mo/tests/test_layers.mojo),
   read from those files as text and recorded with their inputs.
 
-The GPU box never reads /root/reference; the tests only read the JSON.
+The tests only read the JSON; nothing at test time reads the reference tree.
 """
 
 from __future__ import annotations
@@ -25,8 +26,16 @@ from pathlib import Path
 
 import numpy as np
 
-REF = Path("/root/reference")
 HERE = Path(__file__).resolve().parent
+
+
+def _reference_dir() -> Path:
+    if len(sys.argv) != 2:  # noqa: PLR2004
+        sys.exit("usage: python tests/golden/make_golden.py REFERENCE_DIR")
+    return Path(sys.argv[1])
+
+
+REF = _reference_dir() if __name__ == "__main__" else Path()
 
 
 def _import_reference_model():

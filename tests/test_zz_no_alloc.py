@@ -4,7 +4,9 @@ mg_sample_static serves callers that keep all device memory in their own pool
 and cannot have the library call cudaMalloc; its only scratch is a static
 device array shared by every call.  Each case calls it twice in a row on the
 same stream and checks both results against mg_sample's tokens for the same
-logits, sampling arguments and variates (tokens must be identical).
+logits, sampling arguments and variates (tokens must be identical).  One case
+passes rows with a padded stride (ld > vocab), and one checks that repeated
+calls leave the device's free memory unchanged.
 """
 
 from __future__ import annotations
@@ -75,6 +77,43 @@ def test_static_sampler_matches_mg_sample(batch, vocab, temperature, top_k, top_
         assert rc == _core.MG_OK, _lib.mg_last_error().decode()
         torch.cuda.synchronize()
         np.testing.assert_array_equal(out.cpu().numpy(), want)
+
+
+def test_static_sampler_padded_rows() -> None:
+    """Rows of a wider buffer (ld = vocab + 37): the padding holds values that
+    would win the draw if it were read."""
+    torch = pytest.importorskip("torch")
+    batch, vocab, pad = 5, 262144, 37
+    x = _logits(batch, vocab, seed=99)
+    wide = np.full((batch, vocab + pad), 1e4, np.float32)
+    wide[:, :vocab] = x
+    u = np.random.default_rng(5).random(batch)
+    dev = torch.from_numpy(wide).cuda()[:, :vocab]
+    assert dev.stride(0) == vocab + pad
+    du = torch.from_numpy(u).cuda()
+    for temperature, top_k in ((0.0, 0), (0.9, 32)):
+        want = _core.sample(x, temperature, top_k, 1.0, seed=7, offset=3, uniforms=u)
+        for _ in range(2):
+            out = torch.full((batch,), -1, dtype=torch.int32, device="cuda")
+            rc = _static(torch, dev, out, temperature, top_k, 1.0, du, 7, 3)
+            assert rc == _core.MG_OK, _lib.mg_last_error().decode()
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(out.cpu().numpy(), want)
+
+
+def test_static_sampler_leaves_free_memory_unchanged() -> None:
+    torch = pytest.importorskip("torch")
+    batch, vocab = 4, 262144
+    dev = torch.from_numpy(_logits(batch, vocab, seed=3)).cuda()
+    outs = [torch.full((batch,), -1, dtype=torch.int32, device="cuda") for _ in range(8)]
+    assert _static(torch, dev, outs[0], 0.8, 16, 1.0, None, 1, 0) == _core.MG_OK  # first call loads the kernels
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for k, out in enumerate(outs):
+        assert _static(torch, dev, out, 0.8, 16, 1.0, None, 1, k) == _core.MG_OK, _lib.mg_last_error().decode()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
 
 
 def test_static_sampler_rejects_out_of_range() -> None:
