@@ -1,11 +1,17 @@
-"""Safetensors weights as zero-copy host pointers.
+"""Safetensors checkpoints as zero-copy host pointers.
 
-Produces the ``{name: (host_ptr, shape, dtype)}`` metadata that the reference
-loader hands to ``_core.init_model`` (src/py/mogemma/loader.py:86-107): each
-file is memory-mapped read-only and the pointers stay valid while the loader
-is open.  ``init_model`` copies the tensors to HBM once, so the mapping can be
-closed after the model is built.  Orbax/OCDBT checkpoints (converted by the
-reference's convert.py) are outside this engine's scope.
+``_core.init_model`` takes ``{name: (host_ptr, shape, dtype)}`` -- the metadata
+the reference loader produces (src/py/mogemma/loader.py:86-107).  Here every
+shard is memory-mapped read-only and each tensor is described by one table
+entry (shard, byte range, shape, dtype), checked against the shard's size when
+the header is read.  The pointers stay valid while the loader is open;
+``init_model`` copies the tensors to HBM (through pinned staging buffers), so
+the loader can be closed once the model is built.
+
+Accepted layouts: a single ``.safetensors`` file, a directory holding
+``model.safetensors``, or a sharded directory with
+``model.safetensors.index.json``.  Orbax/OCDBT checkpoints are converted by
+``mogemma_b200.convert`` first.
 """
 
 from __future__ import annotations
@@ -13,103 +19,133 @@ from __future__ import annotations
 import json
 import mmap
 import struct
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any, Protocol
 
 import numpy as np
 
+_ITEMSIZE = {"F64": 8, "F32": 4, "F16": 2, "BF16": 2, "I64": 8, "I32": 4, "I16": 2, "I8": 1, "U8": 1, "BOOL": 1,
+             "U16": 2, "U32": 4, "U64": 8, "F8_E4M3": 1, "F8_E5M2": 1}
+_NUMPY = {"F64": np.float64, "F32": np.float32, "F16": np.float16, "I64": np.int64, "I32": np.int32,
+          "I16": np.int16, "I8": np.int8, "U8": np.uint8, "BOOL": np.bool_, "U16": np.uint16, "U32": np.uint32,
+          "U64": np.uint64, "BF16": np.uint16}
+
+
+@dataclass(frozen=True)
+class TensorEntry:
+    """Where one tensor lives: shard index, absolute byte range in the shard, shape, dtype."""
+
+    shard: int
+    begin: int
+    end: int
+    shape: tuple[int, ...]
+    dtype: str
+
 
 class SafetensorsLoader:
-    """Memory-mapped safetensors files exposing raw tensor pointers."""
+    """Read-only memory maps of a checkpoint's shards with a tensor table."""
 
     def __init__(self, model_path: str | Path) -> None:
         self.model_path = Path(model_path)
-        self.mmaps: dict[str, mmap.mmap] = {}
-        self.file_objs: dict[str, Any] = {}
-        self.tensor_file_map: dict[str, str] = {}
-        self.tensor_metadata: dict[str, dict[str, Any]] = {}
-        self.file_data_offsets: dict[str, int] = {}
-        self._bases: dict[str, int] = {}
-        self._views: dict[str, np.ndarray] = {}
-        self._open_all()
+        self._files: list[Any] = []
+        self._maps: list[mmap.mmap] = []
+        self._bytes: list[np.ndarray] = []  # uint8 views of the maps (pointer source)
+        self.tensors: dict[str, TensorEntry] = {}
+        try:
+            for shard in self._shard_paths():
+                self._open_shard(shard)
+        except Exception:
+            self.close()
+            raise
 
-    def _open_all(self) -> None:
+    # ---------------------------------------------------------------- layout
+    def _shard_paths(self) -> list[Path]:
         p = self.model_path
         if p.is_file():
-            self._map(p.name, p)
-            return
+            return [p]
         index = p / "model.safetensors.index.json"
-        if index.exists():
+        if index.is_file():
             weight_map = json.loads(index.read_text(encoding="utf-8")).get("weight_map", {})
-            self.tensor_file_map = dict(weight_map)
-            for fname in sorted(set(weight_map.values())):
-                fpath = p / fname
-                if not fpath.exists():
-                    msg = f"Missing weights file: {fpath}"
-                    raise FileNotFoundError(msg)
-                self._map(fname, fpath)
-            return
-        single = p / "model.safetensors"
-        if not single.exists():
-            msg = f"No model.safetensors or index found in {p}"
-            raise FileNotFoundError(msg)
-        self._map("model.safetensors", single)
+            names = sorted(set(weight_map.values()))
+            missing = [n for n in names if not (p / n).is_file()]
+            if missing:
+                msg = f"Missing weights file: {p / missing[0]}"
+                raise FileNotFoundError(msg)
+            return [p / n for n in names]
+        if (p / "model.safetensors").is_file():
+            return [p / "model.safetensors"]
+        msg = f"No model.safetensors or index found in {p}"
+        raise FileNotFoundError(msg)
 
-    def _map(self, fname: str, fpath: Path) -> None:
-        f = fpath.open("rb")
-        m = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
-        self.file_objs[fname] = f
-        self.mmaps[fname] = m
-        (hlen,) = struct.unpack("<Q", m[:8])
-        header = json.loads(m[8 : 8 + hlen])
-        self.file_data_offsets[fname] = 8 + hlen
-        view = np.frombuffer(m, dtype=np.uint8)
-        self._views[fname] = view
-        self._bases[fname] = int(view.ctypes.data)
+    def _open_shard(self, path: Path) -> None:
+        idx = len(self._maps)
+        f = path.open("rb")
+        self._files.append(f)
+        size = path.stat().st_size
+        if size < 8:  # noqa: PLR2004
+            msg = f"{path}: not a safetensors file ({size} bytes)"
+            raise ValueError(msg)
+        mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+        self._maps.append(mm)
+        (hlen,) = struct.unpack("<Q", mm[:8])
+        if 8 + hlen > size:
+            msg = f"{path}: header of {hlen} bytes runs past the end of the file"
+            raise ValueError(msg)
+        header = json.loads(bytes(mm[8 : 8 + hlen]).decode("utf-8"))
+        self._bytes.append(np.frombuffer(mm, dtype=np.uint8))
+        data0 = 8 + hlen
         for name, meta in header.items():
             if name == "__metadata__":
                 continue
-            self.tensor_file_map[name] = fname
-            self.tensor_metadata[name] = meta
+            dtype = str(meta["dtype"])
+            shape = tuple(int(s) for s in meta["shape"])
+            lo, hi = (int(x) for x in meta["data_offsets"])
+            if not (0 <= lo <= hi and data0 + hi <= size):
+                msg = f"{path}: tensor '{name}' byte range [{lo}, {hi}) lies outside the file"
+                raise ValueError(msg)
+            if dtype in _ITEMSIZE and hi - lo != int(np.prod(shape, dtype=np.int64)) * _ITEMSIZE[dtype]:
+                msg = f"{path}: tensor '{name}' holds {hi - lo} bytes, not {shape} x {dtype}"
+                raise ValueError(msg)
+            self.tensors[name] = TensorEntry(idx, data0 + lo, data0 + hi, shape, dtype)
 
+    # ---------------------------------------------------------------- access
     def get_tensor_metadata(self) -> dict[str, tuple[int, tuple[int, ...], str]]:
-        """``{name: (data_pointer, shape, dtype)}`` for the engine."""
-        out: dict[str, tuple[int, tuple[int, ...], str]] = {}
-        for name, meta in self.tensor_metadata.items():
-            fname = self.tensor_file_map[name]
-            ptr = self._bases[fname] + self.file_data_offsets[fname] + int(meta["data_offsets"][0])
-            out[name] = (ptr, tuple(int(s) for s in meta["shape"]), str(meta["dtype"]))
-        return out
+        """``{name: (host_pointer, shape, dtype)}`` for ``_core.init_model``."""
+        return {name: (int(self._bytes[e.shard].ctypes.data) + e.begin, e.shape, e.dtype)
+                for name, e in self.tensors.items()}
+
+    def array(self, name: str) -> np.ndarray:
+        """A read-only NumPy view of one tensor (BF16 as its raw uint16 bits)."""
+        e = self.tensors[name]
+        return self._bytes[e.shard][e.begin : e.end].view(_NUMPY[e.dtype]).reshape(e.shape)
+
+    @staticmethod
+    def can_load(model_path: Path) -> bool:
+        """True when ``model_path`` holds safetensors weights."""
+        if model_path.is_file():
+            return model_path.suffix == ".safetensors"
+        return (model_path / "model.safetensors").is_file() or (model_path / "model.safetensors.index.json").is_file()
+
+    def close(self) -> None:
+        """Unmap every shard; pointers from get_tensor_metadata become invalid."""
+        self._bytes.clear()
+        for mm in self._maps:
+            try:
+                mm.close()
+            except BufferError:  # a view handed out by array() is still alive
+                pass
+        for f in self._files:
+            f.close()
+        self._maps.clear()
+        self._files.clear()
+        self.tensors.clear()
 
     def __enter__(self) -> SafetensorsLoader:
         return self
 
     def __exit__(self, *exc: object) -> None:
         self.close()
-
-    @staticmethod
-    def can_load(model_path: Path) -> bool:
-        """True when ``model_path`` holds safetensors weights."""
-        if model_path.is_file() and model_path.suffix == ".safetensors":
-            return True
-        if not model_path.is_dir():
-            return False
-        return (model_path / "model.safetensors").exists() or (model_path / "model.safetensors.index.json").exists()
-
-    def close(self) -> None:
-        """Unmap files (pointers from get_tensor_metadata become invalid)."""
-        self._views.clear()
-        for m in self.mmaps.values():
-            try:
-                m.close()
-            except BufferError:
-                pass
-        for f in self.file_objs.values():
-            f.close()
-        self.mmaps.clear()
-        self.file_objs.clear()
-        self.tensor_file_map.clear()
-        self.tensor_metadata.clear()
 
 
 class ModelLoader(Protocol):
@@ -123,7 +159,7 @@ class ModelLoader(Protocol):
 
 
 def auto_loader(model_path: str | Path) -> ModelLoader:
-    """Return a loader for ``model_path`` (safetensors only)."""
+    """A loader for ``model_path`` (safetensors; convert Orbax checkpoints first)."""
     path = Path(model_path)
     if SafetensorsLoader.can_load(path):
         return SafetensorsLoader(path)
