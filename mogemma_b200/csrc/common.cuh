@@ -61,6 +61,57 @@ __device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t *p) {
 }
 __device__ __forceinline__ void set_error(uint32_t *err, uint32_t code) { atomicCAS(err, 0u, code); }
 
+// ---- tagged activations: a float and the tag of the step/layer that wrote it
+// in one 64-bit word, stored and loaded as single-copy-atomic 64-bit accesses.
+// A reader polls the words themselves: a word carrying the expected tag holds
+// the value, so no counter, fence or release is needed between a phase's
+// writers and its readers (one L2 round trip instead of three).
+__device__ __forceinline__ uint64_t tg_pack(float v, uint32_t tag) {
+    return (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ float tg_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+__device__ __forceinline__ uint32_t tg_tag(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
+__device__ __forceinline__ void tg_store(uint64_t *p, float v, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(tg_pack(v, tag)) : "memory");
+}
+__device__ __forceinline__ uint64_t tg_load(const uint64_t *p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// Two adjacent words (16-byte aligned); each element is its own 64-bit access.
+__device__ __forceinline__ void tg_load2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Re-polls the words w[j] (loaded from src(j)) that do not yet carry `tag`
+// until all do.  Bounded like every wait here: false after the budget or once
+// another thread has recorded an error (then the values are not to be used).
+template <int N, typename Src>
+__device__ __forceinline__ bool tg_settle(uint64_t (&w)[N], uint32_t tag, Src src, uint32_t *err, uint32_t site) {
+    auto all = [&]() {
+        bool a = true;
+#pragma unroll
+        for (int j = 0; j < N; ++j) a = a && tg_tag(w[j]) == tag;
+        return a;
+    };
+    if (all()) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; ++n) {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (tg_tag(w[j]) != tag) w[j] = tg_load(src(j));
+        if (all()) return true;
+        if ((n & 7u) == 0u) {
+            if (ld_relaxed_u32(err) != 0u) return false;
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+                set_error(err, kErrTimeoutCounter | site);
+                return false;
+            }
+        }
+    }
+}
+
 // Wait until *ctr >= target (acquire).  Returns false on error/timeout.
 __device__ __forceinline__ bool wait_counter_geq(const uint32_t *ctr, uint32_t target, uint32_t *err,
                                                  uint32_t site) {

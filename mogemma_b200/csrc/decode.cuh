@@ -5,8 +5,9 @@
 // Each CTA is split into 8 consumer warps and 1 producer warp.  The producer
 // streams this CTA's weight tiles (and past K/V rows) through a ring of
 // shared-memory stages with 1-D bulk async copies, running ahead across phase
-// boundaries because weights never depend on activations.  Consumers wait on
-// gpu-scope phase counters for the activations of the previous phase.
+// boundaries because weights never depend on activations.  Consumers poll the
+// previous phase's activations, which are stored as tagged words (value and
+// the tag of the forward and layer that wrote it, in one 64-bit store).
 #pragma once
 
 #include <stdint.h>
@@ -26,6 +27,8 @@ constexpr int kMaxTopK = 64;         // fused top-k width
 constexpr int kAttTile = 16;         // positions per attention tile
 constexpr int kPartHead = 4;         // floats before a split-KV partial's acc: m, l, 2 pad (16-byte aligned acc)
 constexpr int kMaxChunks = 32;       // split-KV chunks per (row, kv head); one warp lane each in the combine
+constexpr int kMaxLayers = 64;       // layers a model may have (tags hold epoch * kMaxLayers + layer)
+constexpr uint32_t kMaxEpoch = (1u << 26) - 1;  // forwards before the tagged buffers are cleared and the count restarts
 
 enum PhaseKind : int { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_D = 4, PH_LMH = 5, PH_SAMPLE = 6 };
 
@@ -74,8 +77,13 @@ struct DecodeParams {
     float *kc, *vc;                                                   // [L][Bmax][Hkv][cap][hdp]
     int64_t kv_layer_stride, kv_row_stride, kv_head_stride;
 
-    float *h, *r, *qkv, *o_raw, *act, *mlp_raw;  // [B][...] activations
-    float *attn_part, *attn_out;
+    // activations [B][...] as tagged words (tg_pack in common.cuh): the value
+    // and the tag of the (forward, layer) that wrote it.  Readers poll the words.
+    // The large vectors that every CTA reads whole stay plain floats behind a
+    // phase counter (doubling their bytes costs more than the counter saves).
+    uint64_t *h, *r, *qkv, *o_raw, *mlp_raw;
+    float *act;         // [B][Ip] GeGLU output
+    float *attn_part;   // split-KV partials [B][Hkv][kMaxChunks][Gq][hd + kPartHead]
     float *logits;      // [B][V]
     uint64_t *cand_key; // [B][G][kMaxTopK] per-CTA top-k keys of the lm_head rows
     float *emb_acc;     // [B][H]
@@ -94,6 +102,8 @@ struct DecodeParams {
     uint64_t seed;
     uint64_t rng_offset;     // Philox counter of this step's draws
 
+    uint32_t epoch;   // forward counter (from 1): words of layer l carry tag epoch * kMaxLayers + l
+    uint32_t pad4_;
     uint32_t *sync;   // phase counters [n_phases], att_done [L], att_cnt [B*Hkv], exit [1]
     uint32_t *err;    // device error word
     int32_t n_phases;

@@ -12,11 +12,15 @@
 //    attention) into a ring of shared-memory stages with cp.async.bulk, ahead
 //    of the consumers and across phase boundaries (weights never depend on
 //    activations).
-//  * Warps 0-7 consume: each phase waits on a gpu-scope counter for its input
-//    activations, builds the normalised input vector in shared memory (RMSNorm
-//    with (1 + w), residual adds), then multiplies it by the staged tiles with
-//    128-bit shared loads and warp-shuffle reductions.  Norm weights and RoPE
-//    rows are loaded before the wait so one L2 round trip follows it.
+//  * Warps 0-7 consume: each phase polls its input activations -- tagged
+//    words (value + tag of the forward and layer that wrote it, one 64-bit
+//    store) written by every CTA in the previous phase -- until each carries
+//    the expected tag, builds the normalised input vector in shared memory
+//    (RMSNorm with (1 + w), residual adds), then multiplies it by the staged
+//    tiles with 128-bit shared loads and warp-shuffle reductions.  Polling the
+//    data itself replaces a counter, its release fence and a second load
+//    round trip per hand-off (measured 1.2 us instead of 2.0 us).  Norm
+//    weights and RoPE rows are loaded before the poll.
 //  * Fusions: input/pre-ff/post-attn/post-ff/final norms and residual adds in
 //    the next phase's prologue; QK-norm, RoPE and the K/V write in the attention
 //    prologue; GeGLU in the gate/up epilogue; the split-KV combine in the
@@ -157,6 +161,11 @@ __device__ __forceinline__ float *att_part(const DecodeParams &p, int b, int kvh
     return p.attn_part + ((static_cast<int64_t>(b) * p.Hkv + kvh) * kMaxChunks + c) * Gq * (p.hd + kPartHead);
 }
 
+// Tag of the words written for `layer` in this forward.
+__device__ __forceinline__ uint32_t tag_of(const DecodeParams &p, int layer) {
+    return p.epoch * static_cast<uint32_t>(kMaxLayers) + static_cast<uint32_t>(layer);
+}
+
 // ---------------------------------------------------------------- shared memory
 struct Smem {
     uint64_t *full;
@@ -231,15 +240,19 @@ __device__ __forceinline__ void norm_prefetch(NormW &nw, const float *w_add, con
 
 // For rows b < NB:  x = base[b] + rmsnorm(add[b]) * (1 + w_add);  out[b] <- x
 // (when out != null);  xs[b] <- rmsnorm(x) * (1 + w_next), zero padded to Kp.
-// base/add rows ([NB][H] in global memory) were written by other CTAs and are
-// read through L2; all loads of a chunk are issued before any is used.
-// XSUM: `add` is nadd per-rank partial blocks (add_stride floats apart) that
-// are summed in rank order, so every rank gets the same bits.
+// base rows ([NB][H] tagged words) and add rows (tagged words add_t, or with
+// XSUM nadd per-rank float blocks add_x, add_stride floats apart, that the
+// caller has already waited for and that are summed in rank order so every
+// rank gets the same bits) were written by other CTAs: all loads of a chunk
+// are issued before any is used, and tagged words are polled until they carry
+// `tag`.  out is written with out_tag.  Returns false if a poll gave up.
 template <int NB, bool XSUM = false>
-__device__ __forceinline__ void stage_norm(const float *base, const float *add, const float *w_add,
-                                           const float *w_next, const NormW &nw, float *out, int H, float inv_h,
-                                           int Kp, float *xs, SmallSmem &ss, int tid, int nadd = 1,
+__device__ __forceinline__ bool stage_norm(const uint64_t *base, const uint64_t *add_t, const float *add_x,
+                                           uint32_t tag, const float *w_add, const float *w_next, const NormW &nw,
+                                           uint64_t *out, uint32_t out_tag, int H, float inv_h, int Kp, float *xs,
+                                           SmallSmem &ss, int tid, uint32_t *err, uint32_t site, int nadd = 1,
                                            int64_t add_stride = 0) {
+    bool ok = true;
     float sq[NB], sq2[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) sq[b] = sq2[b] = 0.f;
@@ -247,36 +260,49 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
     for (int j0 = 0; j0 * kConsumerThreads < H; j0 += kNormPer) {
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-            float v[kNormPer], bv[kNormPer];
+            const uint64_t *brow = base + static_cast<int64_t>(b) * H;
+            const uint64_t *arow = add_t + static_cast<int64_t>(b) * H;
+            uint64_t wb[kNormPer], wa[kNormPer];
+            float v[kNormPer];
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
                 const int i = tid + (j0 + j) * kConsumerThreads;
-                v[j] = i < H ? __ldcg(add + static_cast<int64_t>(b) * H + i) : 0.f;
-                bv[j] = i < H ? __ldcg(base + static_cast<int64_t>(b) * H + i) : 0.f;
+                wb[j] = i < H ? tg_load(brow + i) : tg_pack(0.f, tag);
+                if constexpr (!XSUM) wa[j] = i < H ? tg_load(arow + i) : tg_pack(0.f, tag);
             }
             if constexpr (XSUM) {
-                float t[kMaxTp - 1][kNormPer];
+                float t[kMaxTp][kNormPer];
 #pragma unroll
-                for (int r = 1; r < kMaxTp; ++r)
+                for (int r = 0; r < kMaxTp; ++r)
 #pragma unroll
                     for (int j = 0; j < kNormPer; ++j) {
                         const int i = tid + (j0 + j) * kConsumerThreads;
-                        t[r - 1][j] = (r < nadd && i < H)
-                                          ? __ldcg(add + r * add_stride + static_cast<int64_t>(b) * H + i)
-                                          : 0.f;
+                        t[r][j] = (r < nadd && i < H)
+                                      ? __ldcg(add_x + r * add_stride + static_cast<int64_t>(b) * H + i)
+                                      : 0.f;
                     }
 #pragma unroll
-                for (int r = 1; r < kMaxTp; ++r)
+                for (int j = 0; j < kNormPer; ++j) {
+                    v[j] = t[0][j];
 #pragma unroll
-                    for (int j = 0; j < kNormPer; ++j)
-                        if (r < nadd) v[j] += t[r - 1][j];
+                    for (int r = 1; r < kMaxTp; ++r)
+                        if (r < nadd) v[j] += t[r][j];
+                }
+            }
+            auto bsrc = [&](int j) { return brow + tid + (j0 + j) * kConsumerThreads; };
+            ok = tg_settle(wb, tag, bsrc, err, site) && ok;
+            if constexpr (!XSUM) {
+                auto asrc = [&](int j) { return arow + tid + (j0 + j) * kConsumerThreads; };
+                ok = tg_settle(wa, tag, asrc, err, site) && ok;
+#pragma unroll
+                for (int j = 0; j < kNormPer; ++j) v[j] = tg_val(wa[j]);
             }
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
                 const int i = tid + (j0 + j) * kConsumerThreads;
                 if (i < H) {
                     xs[b * Kp + i] = v[j];
-                    xb[b * H + i] = bv[j];
+                    xb[b * H + i] = tg_val(wb[j]);
                 }
                 sq[b] += v[j] * v[j];
             }
@@ -306,7 +332,7 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
                 if (i < H) {
                     const float x = xb[b * H + i] + xs[b * Kp + i] * inv * (1.0f + wa[j]);
                     xs[b * Kp + i] = x;
-                    if (out) out[static_cast<int64_t>(b) * H + i] = x;
+                    if (out) tg_store(out + static_cast<int64_t>(b) * H + i, x, out_tag);
                     sq2[b] += x * x;
                 }
             }
@@ -336,14 +362,15 @@ __device__ __forceinline__ void stage_norm(const float *base, const float *add, 
         }
     }
     consumer_sync(kConsumerThreads);
+    return ok;
 }
 
 // Layer 0 input: x = E[tok] * sqrt(H) (model.mojo:62-68, layers.mojo:247-251),
 // out <- x, xs <- rmsnorm(x) * (1 + w).
 template <typename WT, int NB>
-__device__ __noinline__ void stage_embed(const WT *E, int64_t ld, const int *toks, const float *w, float *out,
-                                         int H, float inv_h, float scale, int Kp, float *xs, SmallSmem &ss,
-                                         int tid) {
+__device__ __noinline__ void stage_embed(const WT *E, int64_t ld, const int *toks, const float *w, uint64_t *out,
+                                         uint32_t out_tag, int H, float inv_h, float scale, int Kp, float *xs,
+                                         SmallSmem &ss, int tid) {
     float sq[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
@@ -351,7 +378,7 @@ __device__ __noinline__ void stage_embed(const WT *E, int64_t ld, const int *tok
         for (int i = tid; i < H; i += kConsumerThreads) {
             const float x = ld_w(E + static_cast<int64_t>(toks[b]) * ld + i) * scale;
             xs[b * Kp + i] = x;
-            if (out) out[static_cast<int64_t>(b) * H + i] = x;
+            if (out) tg_store(out + static_cast<int64_t>(b) * H + i, x, out_tag);
             s += x * x;
         }
         sq[b] = s;
@@ -374,6 +401,14 @@ __device__ __forceinline__ void cta_signal(uint32_t *ctr, uint32_t n, SmallSmem 
         if (n) red_release_add_u32(ctr, n);
         trace_mark(ss.tr_end);
     }
+}
+
+// End of a phase whose results are tagged words (no counter to count on):
+// the barrier keeps the next prologue from overwriting the shared activation
+// stage while a warp still reads it.
+__device__ __forceinline__ void phase_done(SmallSmem &ss, int tid) {
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) trace_mark(ss.tr_end);
 }
 
 // Wait for a counter; uniform result across consumer threads.
@@ -422,21 +457,33 @@ __device__ __forceinline__ bool xwait(const DecodeParams &p, int which, uint64_t
 
 // ---------------------------------------------------------------- GEMV consumer
 // Where a GEMV phase's row results go: out[b * ld + row] = dot, or with a
-// gate/up pair out[b * ld + row] = gelu_erf(gate) * up (ops.mojo:19-22).
-// With tensor parallelism the partial rows of o_proj / down_proj go to every
-// rank's exchange buffer instead: xdst[k] is rank k's receive block of this
-// rank (nx destinations, nx = 0: local out).
+// gate/up pair out[b * ld + row] = gelu_erf(gate) * up (ops.mojo:19-22), as
+// tagged words (tout, tag) or plain floats (fout: logits).  With tensor
+// parallelism the partial rows of o_proj / down_proj go to every rank's
+// exchange buffer instead: xdst[k] is rank k's receive block of this rank (nx
+// destinations, nx = 0: local out).
 struct GemvOut {
-    float *out;
+    uint64_t *tout;
+    float *fout;
     int64_t ld;
+    uint32_t tag;
     float *const *xdst = nullptr;
     int nx = 0;
 };
+__device__ __forceinline__ GemvOut gemv_out_tagged(uint64_t *out, int64_t ld, uint32_t tag) {
+    return GemvOut{out, nullptr, ld, tag};
+}
+__device__ __forceinline__ GemvOut gemv_out_float(float *out, int64_t ld) { return GemvOut{nullptr, out, ld, 0u}; }
+__device__ __forceinline__ GemvOut gemv_out_peers(float *const *xdst, int nx, int64_t ld) {
+    return GemvOut{nullptr, nullptr, ld, 0u, xdst, nx};
+}
 __device__ __forceinline__ void gemv_store(const GemvOut &o, int64_t idx, float v) {
     if (o.nx) {
         for (int k = 0; k < o.nx; ++k) o.xdst[k][idx] = v;
+    } else if (o.tout) {
+        tg_store(o.tout + idx, v, o.tag);
     } else {
-        o.out[idx] = v;
+        o.fout[idx] = v;
     }
 }
 
@@ -574,7 +621,8 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
             rope_s[b * hd + half + d] = st_[static_cast<int64_t>(ss.pos[b]) * half + d];
         }
     }
-    if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
+    (void)has_dep;  // the q/k/v words are polled below
+    const uint32_t tag = tag_of(p, layer);
     const float scale = p.att_scale;
     const int slot = cta_slot(ph);
     uint32_t done = 0;
@@ -584,27 +632,26 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
         const int pos = ss.pos[b];
         const int t_begin = a.lo[b] + c * p.att_ch;
         const int t_end = min(t_begin + p.att_ch, pos + 1);
-        // ---- raw q (Gq heads), k, v of this kv group: all loads in one round trip
+        // ---- raw q (Gq heads), k, v of this kv group: all loads in one round
+        // trip, polled until every word carries this layer's tag
         {
-            const float *qkv_b = p.qkv + static_cast<int64_t>(b) * p.qkv_rows;
-            constexpr int kPer = (kMaxQPerKv + 2) * kMaxHeadDim / kConsumerThreads;
+            const uint64_t *qkv_b = p.qkv + static_cast<int64_t>(b) * p.qkv_rows;
+            constexpr int kPer = ((GQ ? GQ : kMaxQPerKv) + 2) * (HD ? HD : kMaxHeadDim) / kConsumerThreads + 1;
             const int n = (Gq + 2) * hd;
-            float v[kPer];
+            auto src = [&](int j) {
+                const int i = tid + j * kConsumerThreads;
+                const int vec = i / hd, d = i - vec * hd;
+                return qkv_b + (vec < Gq ? static_cast<int64_t>(kvh * Gq + vec) * hd + d
+                                         : p.A + static_cast<int64_t>((vec == Gq ? 0 : p.Hkv) + kvh) * hd + d);
+            };
+            uint64_t w[kPer];
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) w[j] = tid + j * kConsumerThreads < n ? tg_load(src(j)) : tg_pack(0.f, tag);
+            ok = tg_settle(w, tag, src, p.err, 100 + ph) && ok;
 #pragma unroll
             for (int j = 0; j < kPer; ++j) {
                 const int i = tid + j * kConsumerThreads;
-                int64_t src = 0;
-                if (i < n) {
-                    const int vec = i / hd, d = i - vec * hd;
-                    src = vec < Gq ? static_cast<int64_t>(kvh * Gq + vec) * hd + d
-                                   : p.A + static_cast<int64_t>((vec == Gq ? 0 : p.Hkv) + kvh) * hd + d;
-                }
-                v[j] = i < n ? __ldcg(qkv_b + src) : 0.f;
-            }
-#pragma unroll
-            for (int j = 0; j < kPer; ++j) {
-                const int i = tid + j * kConsumerThreads;
-                if (i < n) q_s[i] = v[j];  // q_s, k_s, v_s are contiguous
+                if (i < n) q_s[i] = tg_val(w[j]);  // q_s, k_s, v_s are contiguous
             }
         }
         if (tid < Gq) {
@@ -1015,9 +1062,10 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
         if (kind == PH_QKV) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
-            float *out_h = (blockIdx.x == 0) ? p.h : nullptr;
+            const uint32_t tag = tag_of(p, layer);
+            uint64_t *out_h = (blockIdx.x == 0) ? p.h : nullptr;
             if (layer == 0) {
-                stage_embed<WT, NB>(static_cast<const WT *>(p.embed), p.embed_ld, ss.tok, lp.in_ln, out_h, p.H,
+                stage_embed<WT, NB>(static_cast<const WT *>(p.embed), p.embed_ld, ss.tok, lp.in_ln, out_h, tag, p.H,
                                     p.inv_h, p.emb_scale, g.Kp, sm.xs, ss, tid);
             } else {
                 const LayerPtrs &prev = sm.layers[layer - 1];
@@ -1026,17 +1074,18 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                 // x = r + norm(mlp, post_ff) (layers.mojo:216-220), xs = norm(x, input_layernorm) (195)
                 if constexpr (TP) {  // mlp = the sum of every rank's down_proj partial of layer - 1
                     ok = xwait(p, 1, p.xep + layer - 1, 100 + ph, ss, tid) && ok;
-                    stage_norm<NB, true>(p.r, xrecv(p, p.tp_rank, 1), prev.post_ff_ln, lp.in_ln, nw, out_h, p.H,
-                                         p.inv_h, g.Kp, sm.xs, ss, tid, p.tp, static_cast<int64_t>(p.xB) * p.H);
+                    ok = stage_norm<NB, true>(p.r, nullptr, xrecv(p, p.tp_rank, 1), tag - 1, prev.post_ff_ln,
+                                              lp.in_ln, nw, out_h, tag, p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.err,
+                                              100 + ph, p.tp, static_cast<int64_t>(p.xB) * p.H) && ok;
                 } else {
-                    if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
-                    stage_norm<NB>(p.r, p.mlp_raw, prev.post_ff_ln, lp.in_ln, nw, out_h, p.H, p.inv_h, g.Kp, sm.xs,
-                                   ss, tid);
+                    ok = stage_norm<NB>(p.r, p.mlp_raw, nullptr, tag - 1, prev.post_ff_ln, lp.in_ln, nw, out_h, tag,
+                                        p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.err, 100 + ph) && ok;
                 }
             }
+            if (tid == 0) trace_mark(ss.tr_ready);
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                             GemvOut{p.qkv, p.qkv_rows});
-            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+                                 gemv_out_tagged(p.qkv, p.qkv_rows, tag));
+            phase_done(ss, tid);
         } else if (kind == PH_ATT) {
             if (tid == 0) att_rows<NB>(p, lp.is_global != 0, ss.pos, ss.att);
             consumer_sync(kConsumerThreads);
@@ -1047,39 +1096,43 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
         } else if (kind == PH_O) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
+            const uint32_t tag = tag_of(p, layer);
             if (tid == 0) att_rows<NB>(p, lp.is_global != 0, ss.pos, ss.att);
             consumer_sync(kConsumerThreads);
-            const AttRows &a = ss.att;
             if (has_dep)
-                ok = cta_wait(ctr_phase(p, ph - 1), static_cast<uint32_t>(a.nitems), p.err, 100 + ph, ss, tid) && ok;
-            att_combine(p, a, g.Kp, sm.xs, tid);
+                ok = cta_wait(ctr_phase(p, ph - 1), static_cast<uint32_t>(ss.att.nitems), p.err, 100 + ph, ss, tid) &&
+                     ok;
+            att_combine(p, ss.att, g.Kp, sm.xs, tid);
             // with tensor parallelism the row-split o_proj partials go to every rank
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                                 TP ? GemvOut{nullptr, p.H, ss.xdst_o, p.tp} : GemvOut{p.o_raw, p.H});
-            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+                                 TP ? gemv_out_peers(ss.xdst_o, p.tp, p.H) : gemv_out_tagged(p.o_raw, p.H, tag));
+            phase_done(ss, tid);
             if constexpr (TP) xsignal(p, 0, tid);
         } else if (kind == PH_GU) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
+            const uint32_t tag = tag_of(p, layer);
             NormW nw;
             norm_prefetch(nw, lp.post_attn_ln, lp.pre_ff_ln, p.H, tid);
+            uint64_t *out_r = blockIdx.x == 0 ? p.r : nullptr;
             // r = h + norm(o_raw, post_attn) (layers.mojo:202-207); xs = norm(r, pre_ff) (209-210)
             if constexpr (TP) {  // o_raw = the sum of every rank's o_proj partial
                 ok = xwait(p, 0, p.xep + layer, 100 + ph, ss, tid) && ok;
-                stage_norm<NB, true>(p.h, xrecv(p, p.tp_rank, 0), lp.post_attn_ln, lp.pre_ff_ln, nw,
-                                     blockIdx.x == 0 ? p.r : nullptr, p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.tp,
-                                     static_cast<int64_t>(p.xB) * p.H);
+                ok = stage_norm<NB, true>(p.h, nullptr, xrecv(p, p.tp_rank, 0), tag, lp.post_attn_ln, lp.pre_ff_ln,
+                                          nw, out_r, tag, p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.err, 100 + ph, p.tp,
+                                          static_cast<int64_t>(p.xB) * p.H) && ok;
             } else {
-                if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
-                stage_norm<NB>(p.h, p.o_raw, lp.post_attn_ln, lp.pre_ff_ln, nw, blockIdx.x == 0 ? p.r : nullptr,
-                               p.H, p.inv_h, g.Kp, sm.xs, ss, tid);
+                ok = stage_norm<NB>(p.h, p.o_raw, nullptr, tag, lp.post_attn_ln, lp.pre_ff_ln, nw, out_r, tag, p.H,
+                                    p.inv_h, g.Kp, sm.xs, ss, tid, p.err, 100 + ph) && ok;
             }
+            if (tid == 0) trace_mark(ss.tr_ready);
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                             GemvOut{p.act, p.Ip});
+                                 gemv_out_float(p.act, p.Ip));
             cta_signal(ctr_phase(p, ph), 1u, ss, tid);
         } else if (kind == PH_D) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
+            const uint32_t tag = tag_of(p, layer);
             if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
             // down_proj input: act rows, 8 float4 loads in flight per thread
             for (int b = 0; b < B; ++b) {
@@ -1100,8 +1153,8 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             }
             consumer_sync(kConsumerThreads);
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                                 TP ? GemvOut{nullptr, p.H, ss.xdst_d, p.tp} : GemvOut{p.mlp_raw, p.H});
-            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+                                 TP ? gemv_out_peers(ss.xdst_d, p.tp, p.H) : gemv_out_tagged(p.mlp_raw, p.H, tag));
+            phase_done(ss, tid);
             if constexpr (TP) xsignal(p, 1, tid);
         } else if (kind == PH_LMH) {
             GemvGeom<WT> g;
@@ -1110,14 +1163,15 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                 NormW nw;
                 norm_prefetch(nw, lp.post_ff_ln, p.final_norm, p.H, tid);
                 // x = r + norm(mlp_raw, post_ff); xs = norm(x, final norm) (layers.mojo:283-285)
+                const uint32_t tag = tag_of(p, p.L - 1);
                 if constexpr (TP) {
                     ok = xwait(p, 1, p.xep + p.L - 1, 100 + ph, ss, tid) && ok;
-                    stage_norm<NB, true>(p.r, xrecv(p, p.tp_rank, 1), lp.post_ff_ln, p.final_norm, nw, nullptr,
-                                         p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.tp, static_cast<int64_t>(p.xB) * p.H);
+                    ok = stage_norm<NB, true>(p.r, nullptr, xrecv(p, p.tp_rank, 1), tag, lp.post_ff_ln, p.final_norm,
+                                              nw, nullptr, 0u, p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.err, 100 + ph,
+                                              p.tp, static_cast<int64_t>(p.xB) * p.H) && ok;
                 } else {
-                    if (has_dep) ok = cta_wait(ctr_phase(p, ph - 1), G, p.err, 100 + ph, ss, tid) && ok;
-                    stage_norm<NB>(p.r, p.mlp_raw, lp.post_ff_ln, p.final_norm, nw, nullptr, p.H, p.inv_h, g.Kp,
-                                   sm.xs, ss, tid);
+                    ok = stage_norm<NB>(p.r, p.mlp_raw, nullptr, tag, lp.post_ff_ln, p.final_norm, nw, nullptr, 0u,
+                                        p.H, p.inv_h, g.Kp, sm.xs, ss, tid, p.err, 100 + ph) && ok;
                 }
             }
             if (p.lm_mode == kLmEmbed) {
@@ -1128,7 +1182,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                                 p.emb_acc[static_cast<int64_t>(b) * p.H + i] += sm.xs[b * g.Kp + i];
             } else if (p.lm_mode == kLmLogits) {
                 gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                                 GemvOut{p.logits, p.V});
+                                     gemv_out_float(p.logits, p.V));
                 if (p.topk > 0) {
                     consumer_sync(kConsumerThreads);
                     lm_topk(p, sm, g.row0, g.nrows, tid);

@@ -126,8 +126,12 @@ struct mg_model {
     float *cos_l = nullptr, *sin_l = nullptr, *cos_g = nullptr, *sin_g = nullptr;
     float *kc = nullptr, *vc = nullptr;
     int64_t kv_layer_stride = 0, kv_row_stride = 0, kv_head_stride = 0;
-    float *h = nullptr, *r = nullptr, *qkv = nullptr, *o_raw = nullptr, *act = nullptr, *mlp_raw = nullptr;
-    float *attn_part = nullptr, *attn_out = nullptr, *logits = nullptr, *emb_acc = nullptr;
+    // decode activations as tagged words (value + tag of the forward and layer that wrote them)
+    uint64_t *h = nullptr, *r = nullptr, *qkv = nullptr, *o_raw = nullptr, *mlp_raw = nullptr;
+    size_t tagged_words = 0;   // h .. mlp_raw, allocated as one block
+    float *act = nullptr, *attn_part = nullptr;
+    uint32_t epoch = 0;        // forwards run so far (tags of the next one use epoch + 1)
+    float *logits = nullptr, *emb_acc = nullptr;
     uint64_t *cand_key = nullptr;
     int32_t *tok = nullptr, *pos = nullptr, *ids = nullptr, *nvalid = nullptr, *out_tokens = nullptr;
     int64_t ids_cap = 0, out_cap = 0;
@@ -353,6 +357,7 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     int L = 0;
     while (find(d, "model.layers." + std::to_string(L) + ".input_layernorm.weight")) ++L;
     if (L == 0) return fail(MG_ERR_INVALID, "Invalid standard model weights: no layers found in metadata");
+    if (L > kMaxLayers) return fail(MG_ERR_UNSUPPORTED, "%d layers (at most %d)", L, kMaxLayers);
     auto lw = [&](int l, const char *k) { return find(d, "model.layers." + std::to_string(l) + "." + k); };
     const Desc *qn0 = lw(0, "self_attn.q_norm.weight");
     int hd = (qn0 && !qn0->shape.empty() && qn0->shape[0] > 0) ? static_cast<int>(qn0->shape[0]) : 256;
@@ -672,14 +677,24 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     TRY(dalloc(m, &m->vc, static_cast<size_t>(m->kv_layer_stride) * L));
     // ---- activations
     const int B = m->Bmax;
-    TRY(dalloc(m, &m->h, static_cast<size_t>(B) * m->H));
-    TRY(dalloc(m, &m->r, static_cast<size_t>(B) * m->H));
-    TRY(dalloc(m, &m->qkv, static_cast<size_t>(B) * m->qkv_rows));
-    TRY(dalloc(m, &m->o_raw, static_cast<size_t>(B) * m->H));
+    {  // one zeroed block (tag 0 is never expected), each part 256-byte aligned
+        const size_t sizes[5] = {static_cast<size_t>(B) * m->H, static_cast<size_t>(B) * m->H,
+                                 static_cast<size_t>(B) * m->qkv_rows, static_cast<size_t>(B) * m->H,
+                                 static_cast<size_t>(B) * m->H};
+        size_t total = 0;
+        for (size_t n : sizes) total += (n + 31) / 32 * 32;
+        uint64_t *blk = nullptr;
+        TRY(dalloc(m, &blk, total));
+        m->tagged_words = total;
+        uint64_t **dst[5] = {&m->h, &m->r, &m->qkv, &m->o_raw, &m->mlp_raw};
+        size_t off = 0;
+        for (int k = 0; k < 5; ++k) {
+            *dst[k] = blk + off;
+            off += (sizes[k] + 31) / 32 * 32;
+        }
+    }
     TRY(dalloc(m, &m->act, static_cast<size_t>(B) * m->Ip));
-    TRY(dalloc(m, &m->mlp_raw, static_cast<size_t>(B) * m->H));
     TRY(dalloc(m, &m->attn_part, static_cast<size_t>(B) * m->Hkv * m->max_ch * Gq * (hd + kPartHead)));
-    TRY(dalloc(m, &m->attn_out, static_cast<size_t>(B) * m->Ap));
     if (m->tp > 1) {
         // exchange buffer: counters, o_proj / down_proj partials [tp][Bmax][H],
         // lm_head candidates [tp][Bmax][G][kMaxTopK], this rank's logits [Bmax][V]
@@ -802,7 +817,6 @@ static DecodeParams base_params(mg_model *m, int B) {
     p.act = m->act;
     p.mlp_raw = m->mlp_raw;
     p.attn_part = m->attn_part;
-    p.attn_out = m->attn_out;
     p.logits = m->logits;
     p.cand_key = m->cand_key;
     p.emb_acc = m->emb_acc;
@@ -845,6 +859,13 @@ static mg_status run_decode(mg_model *m, DecodeParams &p, int max_ctx) {
     if (m->tp > 1 && !m->tp_connected)
         return fail(MG_ERR_INVALID, "tensor-parallel model used before mg_tp_connect");
     p.att_ch = att_chunk(m, p.B, max_ctx);
+    // every forward writes its activations with new tags; before the count
+    // wraps, the words are cleared so that no old tag can match again
+    if (++m->epoch > kMaxEpoch) {
+        CU(cudaMemsetAsync(m->h, 0, m->tagged_words * sizeof(uint64_t), m->stream));
+        m->epoch = 1;
+    }
+    p.epoch = m->epoch;
     const bool persistent = m->decode_path == 0;
     if (persistent) {
         cudaError_t e = m->wdtype == MG_F32 ? decode_launch<float>(p, m->G, m->smem, m->stream, true)
