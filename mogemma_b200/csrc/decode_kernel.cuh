@@ -589,6 +589,9 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
                                          bool has_dep) {
     constexpr int kQ = GQ ? GQ : kMaxQPerKv;         // accumulator slots
     constexpr int kDL = HD ? HD / 32 : kMaxHeadDim / 32;  // head dims per lane
+    // Head dims 64/128/256 whose q heads x dims fill whole 256-thread rounds take
+    // the two-tile pass below; other shapes keep the tile-at-a-time loop.
+    constexpr bool kFast = (HD == 64 || HD == 128 || HD == 256) && GQ > 0 && (GQ * HD) % kConsumerThreads == 0;
     const int G = gridDim.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int Gq = GQ ? GQ : p.Hq / p.Hkv;
@@ -596,12 +599,13 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
     const int half = hd / 2;
     const int B = p.B;
     const int hdp = HD ? HD : p.hdp;
-    // shared scratch: q [Gq][hd], k, v, scores [Gq][kAttTile], m/l/alpha, norm weights, rope rows [B][hd]
+    // shared scratch: q [Gq][hd], k, v, scores [Gq][2 * kAttTile], m/l/alpha, norm weights,
+    // rope rows [B][hd], then the P.V reduction block
     float *q_s = sm.xs;
     float *k_s = q_s + Gq * hd;
     float *v_s = k_s + hd;
     float *sc = v_s + hd;
-    float *m_s = sc + Gq * kAttTile;
+    float *m_s = sc + Gq * 2 * kAttTile;
     float *l_s = m_s + kMaxQPerKv;
     float *al_s = l_s + kMaxQPerKv;
     float *qn_s = al_s + kMaxQPerKv;
@@ -704,6 +708,139 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
                 p.vc[off + d] = v_s[d];
             }
         }
+        if constexpr (kFast) {
+            // Groups of two tiles (32 positions) at a time, one pass each:
+            //  scores  thread (position sp, dim slice sl): float4 dims 4 sl + 32 j of
+            //          its key row against every q head, reduced over the 8 slices
+            //          with 3 shuffles;
+            //  softmax one warp per head, lane = position (online across groups);
+            //  P.V     thread (dims 4 dq .. 4 dq + 3, position class pq): kPPQ
+            //          positions, every head; classes summed through shared memory
+            //          into the running accumulators run[] (outputs tid + 256 k).
+            constexpr int kGP = 2 * kAttTile;
+            constexpr int kDG = HD / 4;
+            constexpr int kNPQ = kConsumerThreads / kDG;
+            constexpr int kPPQ = kGP / kNPQ;
+            constexpr int kOut = GQ * HD / kConsumerThreads;
+            float *red = rope_s + B * hd;  // [kNPQ][GQ][HD]
+            float run[kOut];
+#pragma unroll
+            for (int k = 0; k < kOut; ++k) run[k] = 0.f;
+            const int sp = tid >> 3, sl = tid & 7;
+            const int dq = tid % kDG, pq = tid / kDG;
+            for (int ts = t_begin; ts < t_end; ts += kGP) {
+                const int np = min(kGP, t_end - ts);
+                const int ntl = (np + kAttTile - 1) / kAttTile;
+                const float *kt[2], *vt[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const uint32_t tu = tile + static_cast<uint32_t>(min(u, ntl - 1));
+                    const int st = static_cast<int>(tu % p.S);
+                    if (u < ntl && ok) ok = mbar_wait(&sm.full[st], (tu / p.S) & 1u, p.err, kErrTimeoutFull | 2u);
+                    kt[u] = reinterpret_cast<const float *>(sm.ring + static_cast<size_t>(st) * kStageBytes);
+                    vt[u] = kt[u] + kAttTile * HD;
+                }
+                if (tid == 0 && done == 0 && ts == t_begin) trace_mark(trace_slot(p, ph, kTrPrologue));
+                {
+                    float acc[GQ];
+#pragma unroll
+                    for (int h = 0; h < GQ; ++h) acc[h] = 0.f;
+                    if (sp < np) {
+                        const float *kr = (ts + sp == pos) ? k_s : kt[sp >> 4] + (sp & 15) * HD;
+#pragma unroll
+                        for (int j = 0; j < HD / 32; ++j) {
+                            const int d = 4 * sl + 32 * j;
+                            const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+#pragma unroll
+                            for (int h = 0; h < GQ; ++h) {
+                                const float4 q4 = *reinterpret_cast<const float4 *>(q_s + h * HD + d);
+                                acc[h] += q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int h = 0; h < GQ; ++h) {
+                        acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+                        acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
+                        acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 4);
+                    }
+                    if (sl == 0) {
+#pragma unroll
+                        for (int h = 0; h < GQ; ++h) sc[h * kGP + sp] = sp < np ? acc[h] * scale : -INFINITY;
+                    }
+                }
+                consumer_sync(kConsumerThreads);
+                if (warp < GQ) {  // online softmax bookkeeping (ops.mojo:139-182), lane = position
+                    const int h = warp;
+                    const float sv = sc[h * kGP + lane];
+                    const float m_old = m_s[h];
+                    const float m_new = fmaxf(m_old, warp_max(sv));
+                    const float e = lane < np ? expf(sv - m_new) : 0.f;
+                    sc[h * kGP + lane] = e;
+                    const float es = warp_sum(e);
+                    if (lane == 0) {
+                        const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+                        al_s[h] = alpha;
+                        l_s[h] = l_s[h] * alpha + es;
+                        m_s[h] = m_new;
+                    }
+                }
+                consumer_sync(kConsumerThreads);
+                {  // P @ V (layers.mojo:89-94)
+                    float4 a4[GQ];
+#pragma unroll
+                    for (int h = 0; h < GQ; ++h) a4[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < kPPQ; ++i) {
+                        const int pp = pq * kPPQ + i;
+                        if (pp < np) {
+                            const float *vr = (ts + pp == pos) ? v_s : vt[pp >> 4] + (pp & 15) * HD;
+                            const float4 v4 = *reinterpret_cast<const float4 *>(vr + 4 * dq);
+#pragma unroll
+                            for (int h = 0; h < GQ; ++h) {
+                                const float pr = sc[h * kGP + pp];
+                                a4[h].x += pr * v4.x;
+                                a4[h].y += pr * v4.y;
+                                a4[h].z += pr * v4.z;
+                                a4[h].w += pr * v4.w;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int h = 0; h < GQ; ++h) *reinterpret_cast<float4 *>(red + (pq * GQ + h) * HD + 4 * dq) = a4[h];
+                }
+                __syncwarp();
+                if (lane == 0)
+                    for (int u = 0; u < ntl; ++u) mbar_arrive(&sm.empty[(tile + u) % p.S]);
+                tile += static_cast<uint32_t>(ntl);
+                consumer_sync(kConsumerThreads);
+#pragma unroll
+                for (int k = 0; k < kOut; ++k) {
+                    const int o = tid + k * kConsumerThreads;
+                    const int h = o / HD, d = o - h * HD;
+                    float sum = 0.f;
+#pragma unroll
+                    for (int q = 0; q < kNPQ; ++q) sum += red[(q * GQ + h) * HD + d];
+                    run[k] = run[k] * al_s[h] + sum;
+                }
+                consumer_sync(kConsumerThreads);
+            }
+            if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttTiles));
+            // ---- partial (m, l, acc) of this chunk; combined in the o_proj prologue
+            float *part = att_part(p, b, kvh, c);
+            const int part_ld = hd + kPartHead;
+#pragma unroll
+            for (int k = 0; k < kOut; ++k) {
+                const int o = tid + k * kConsumerThreads;
+                const int h = o / HD, d = o - h * HD;
+                part[h * part_ld + kPartHead + d] = run[k];
+            }
+            if (tid < Gq) {
+                part[tid * part_ld + 0] = m_s[tid];
+                part[tid * part_ld + 1] = l_s[tid];
+            }
+            consumer_sync(kConsumerThreads);
+        } else {
         // P.V ownership: thread -> head dim pv_d, position class pv_q of ntq
         const int ntq = kConsumerThreads / hd;
         const int pv_d = tid % hd, pv_q = tid / hd;
@@ -823,6 +960,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
             part[tid * part_ld + 1] = l_s[tid];
         }
         consumer_sync(kConsumerThreads);
+        }
         if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttPart));
         ++done;
     }

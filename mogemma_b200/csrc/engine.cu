@@ -471,8 +471,10 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         int xs = Bd * Kmax;
         xs = std::max(xs, Bd * (m->Hp + m->H));  // normed input + staged residual rows
         xs = std::max(xs, Bd * (m->Ap + m->Hq * kMaxChunks));
-        xs = std::max(xs, (Gq + 2) * hd + Gq * kAttTile + 3 * kMaxQPerKv + 2 * hd + Bd * hd + kConsumerThreads * Gq +
-                              8);
+        // attention: q, k, v, scores of two tiles, m/l/alpha, q/k norm weights, RoPE rows,
+        // then the P.V reduction block (1024 * Gq floats in the two-tile pass)
+        xs = std::max(xs, (Gq + 2) * hd + Gq * 2 * kAttTile + 3 * kMaxQPerKv + 2 * hd + Bd * hd +
+                              std::max(kConsumerThreads, 1024) * Gq + 8);
         xs = std::max(xs, static_cast<int>((sizeof(uint32_t) * 264 + sizeof(uint64_t) * 1024 + kMaxTopK * 8 * 2 +
                                             kMaxTopK * 4) / 4 + 16));
         return (xs + 31) / 32 * 32;
