@@ -432,6 +432,18 @@ def step_rows(llm: dict[str, Any], token_ids: Sequence[int], *, logits: bool = T
     return lg, out
 
 
+def set_row_pos(llm: dict[str, Any], row: int, pos: int) -> None:
+    """Set one row's next position (a stream reusing a row restarts it at 0)."""
+    h = _handle(llm)
+    h.set_pos(int(pos), row=int(row))
+    llm["pos"] = h.pos  # llm["pos"] mirrors row 0
+
+
+def row_positions(llm: dict[str, Any]) -> list[int]:
+    """Next position of every row."""
+    return _handle(llm).get_pos()
+
+
 def prefill_rows(llm: dict[str, Any], rows: Sequence[Sequence[int]]) -> None:
     """Prefill several rows (ragged) at their current positions."""
     h = _handle(llm)

@@ -128,10 +128,12 @@ def _resolve_model_path(raw_model_path: str | Path) -> Path:
     return HubManager().resolve_model(str(raw_model_path), download_if_missing=True, strict=True)
 
 
-def _initialize_llm(loader: ModelLoader, *, model_type: str) -> object:
+def _initialize_llm(loader: ModelLoader, *, model_type: str, rows: int = 1) -> object:
     if _core is None:
         raise _core_missing(model_type)
     try:
+        if rows > 1 and hasattr(_core, "step_rows"):  # the CUDA engine: a model with several rows
+            return _core.init_model(loader.get_tensor_metadata(), max_batch=rows)
         return _core.init_model(loader.get_tensor_metadata())
     except Exception as exc:
         msg = f"{model_type} model failed to initialize from '{loader.model_path}': {exc}"
@@ -249,7 +251,8 @@ class EmbeddingModel:
 class SyncGemmaModel:
     """Gemma 3 text generation on the CUDA engine."""
 
-    def __init__(self, config: GenerationConfig | str | None = None, tokenizer: _Tokenizer | None = None) -> None:
+    def __init__(self, config: GenerationConfig | str | None = None, tokenizer: _Tokenizer | None = None, *,
+                 _rows: int = 1) -> None:
         if config is None:
             config = GenerationConfig()
         elif isinstance(config, str):
@@ -259,7 +262,7 @@ class SyncGemmaModel:
         self.model_path = _resolve_model_path(config.model_path)
         self._loader = auto_loader(self.model_path)
         self._instruction_tuned = _is_instruction_tuned_model(self.model_path, config.model_path)
-        self._llm: object | None = _initialize_llm(self._loader, model_type="generation")
+        self._llm: object | None = _initialize_llm(self._loader, model_type="generation", rows=_rows)
 
     def _ensure_tokenizer(self) -> _Tokenizer:
         if self._tokenizer is not None:
@@ -329,15 +332,53 @@ class SyncGemmaModel:
 
 
 class AsyncGemmaModel:
-    """asyncio wrapper: each step of the sync generator runs in a worker thread."""
+    """asyncio front end of SyncGemmaModel.
 
-    def __init__(self, config: GenerationConfig | str | None = None) -> None:
-        self._model = SyncGemmaModel(config)
+    With the CUDA engine, concurrent ``generate_stream`` calls are batched onto
+    one device model (``serving.BatchScheduler``): each stream gets a row, and
+    one decode launch per step advances every live stream, each at its own
+    position.  With a backend that only offers the reference trio
+    (init_model / step / generate_embeddings), streams run one at a time in a
+    worker thread, as the reference does (src/py/mogemma/model.py:379-420).
+    """
+
+    MAX_CONCURRENT = 8  # streams decoded together (rows of the persistent decode kernel)
+
+    def __init__(self, config: GenerationConfig | str | None = None, *, max_concurrent: int | None = None) -> None:
+        rows = self.MAX_CONCURRENT if max_concurrent is None else max(1, int(max_concurrent))
+        self._model = SyncGemmaModel(config, _rows=rows)
+        self._rows = rows
+        self._scheduler: Any = None
+
+    def _batcher(self) -> Any:
+        """The scheduler when the backend is the CUDA engine with several rows, else None."""
+        core = _core
+        llm = self._model._llm  # noqa: SLF001
+        if self._rows < 2 or core is None or not hasattr(core, "set_row_pos") or not isinstance(llm, dict):
+            return None
+        if self._scheduler is None:
+            from .serving import BatchScheduler  # noqa: PLC0415
+
+            tokenizer = self._model._ensure_tokenizer()  # noqa: SLF001
+            cfg = self._model.config
+            self._scheduler = BatchScheduler(
+                core=core, llm=llm, rows=self._rows, decode=lambda t: tokenizer.decode([t]),
+                eos=_normalize_eos_token_id(tokenizer), max_tokens=cfg.max_tokens,
+                sampling=(cfg.temperature, cfg.top_k, cfg.top_p), capacity=int(llm["max_seq_len"]))
+        return self._scheduler
 
     async def generate(self, prompt: str) -> str:
+        if self._batcher() is not None:
+            return "".join([piece async for piece in self.generate_stream(prompt)])
         return await asyncio.to_thread(self._model.generate, prompt)
 
     async def generate_stream(self, prompt: str) -> AsyncIterator[str]:
+        batcher = self._batcher()
+        if batcher is not None:
+            tokens = self._model._prompt_tokens(self._model._ensure_tokenizer(), prompt)  # noqa: SLF001
+            async for piece in batcher.stream(tokens):
+                yield piece
+            return
         gen = self._model.generate_stream(prompt)
 
         def pull() -> str | None:
@@ -358,6 +399,12 @@ class AsyncGemmaModel:
         finally:
             with contextlib.suppress(RuntimeError):
                 gen.close()
+
+    def close(self) -> None:
+        """Stop the batching worker (streams still waiting get an error)."""
+        if self._scheduler is not None:
+            self._scheduler.close()
+            self._scheduler = None
 
     @property
     def tokenizer(self) -> _Tokenizer:
