@@ -1129,14 +1129,21 @@ static __device__ __noinline__ void lm_topk(const DecodeParams &p, const Smem &s
 }
 
 // Merge of all CTAs' candidates for row b and the draw (model.py:103-150).
-// Candidates are staged in the idle ring with batched loads first.
+// Every CTA's list holds its K best keys, sorted.  For K > kHead the K best
+// of all lists are first looked for among the heads (first kHead keys) of the
+// lists: they are the true K best whenever the K-th of them beats every list's
+// next key (key kHead), which holds unless one list holds more than kHead of
+// the winners; otherwise all keys are merged.  Keys are staged in the idle ring.
 static __device__ __noinline__ int32_t row_draw(const DecodeParams &p, const Smem &sm, int b, bool ok, int tid) {
+    constexpr int kHead = 8;
     const int G = gridDim.x;
     SelectSmem &sel = *reinterpret_cast<SelectSmem *>(sm.xs);
     unsigned char *after = reinterpret_cast<unsigned char *>(sm.xs) + sizeof(SelectSmem);
     uint64_t *outk = reinterpret_cast<uint64_t *>(after);
     double *fscr = reinterpret_cast<double *>(after + kMaxTopK * sizeof(uint64_t));
-    int *oscr = reinterpret_cast<int *>(fscr + kMaxTopK);
+    double *escr = fscr + kMaxTopK;
+    int *oscr = reinterpret_cast<int *>(escr + kMaxTopK);
+    int *ish = oscr + kMaxTopK;  // [4]
     // candidates (rank s, CTA g, k): tp = 1 reads this rank's cand_key; tp > 1
     // the exchange block that every rank wrote its CTAs' candidates into
     const uint64_t *ck = p.tp > 1 ? reinterpret_cast<const uint64_t *>(p.xpeer[p.tp_rank] + p.x_cand) +
@@ -1144,40 +1151,85 @@ static __device__ __noinline__ int32_t row_draw(const DecodeParams &p, const Sme
                                   : p.cand_key + static_cast<int64_t>(b) * G * kMaxTopK;
     const int64_t sstride = static_cast<int64_t>(p.xB) * G * kMaxTopK;
     const int K = p.topk;
-    const int GK = G * K;
-    const int n = p.tp * GK;
-    auto cand_at = [&](int i) {
-        const int s = i / GK, r = i - s * GK;
-        return __ldcg(ck + s * sstride + (r / K) * kMaxTopK + (r % K));
+    const int nl = p.tp * G;  // lists
+    auto list = [&](int l) {
+        const int s = l / G, g = l - s * G;
+        return ck + s * sstride + static_cast<int64_t>(g) * kMaxTopK;
     };
-    if (static_cast<size_t>(n) * sizeof(uint64_t) > static_cast<size_t>(p.S) * kStageBytes) {  // ring too small
-        block_select_topk(
-            n, K, cand_at, outk, sel, tid, kConsumerThreads, [] { consumer_sync(kConsumerThreads); });
-    } else {
+    auto sync = [] { consumer_sync(kConsumerThreads); };
     uint64_t *keys = reinterpret_cast<uint64_t *>(sm.ring);
-    for (int i0 = 0; i0 < n; i0 += 16 * kConsumerThreads) {
-        uint64_t v[16];
+    bool merged = false;
+    if (K > kHead && static_cast<size_t>(nl) * (kHead + 1) * sizeof(uint64_t) <= static_cast<size_t>(p.S) * kStageBytes) {
+        uint64_t *nxt = keys + nl * kHead;  // key kHead of every list
+        const int tot = nl * (kHead + 1);
+        for (int i0 = 0; i0 < tot; i0 += 8 * kConsumerThreads) {
+            uint64_t v[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int i = i0 + tid + j * kConsumerThreads;
-            v[j] = i < n ? cand_at(i) : 0ull;
-        }
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + tid + j * kConsumerThreads;
+                v[j] = i < tot ? __ldcg(list(i / (kHead + 1)) + i % (kHead + 1)) : 0ull;
+            }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int i = i0 + tid + j * kConsumerThreads;
-            if (i < n) keys[i] = v[j];
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + tid + j * kConsumerThreads;
+                if (i < tot) {
+                    const int l = i / (kHead + 1), k = i - l * (kHead + 1);
+                    if (k < kHead) keys[l * kHead + k] = v[j];
+                    else nxt[l] = v[j];
+                }
+            }
+        }
+        sync();
+        block_select_topk(nl * kHead, K, [&](int i) { return keys[i]; }, outk, sel, tid, kConsumerThreads, sync);
+        uint64_t m = 0;
+        for (int l = tid; l < nl; l += kConsumerThreads) m = nxt[l] > m ? nxt[l] : m;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t other = __shfl_xor_sync(0xffffffffu, m, o);
+            m = other > m ? other : m;
+        }
+        if ((tid & 31) == 0) sel.tmp[tid >> 5] = m;
+        sync();
+        if (tid == 0) {
+            uint64_t mx = 0;
+            for (int w = 0; w < kConsumerWarps; ++w) mx = sel.tmp[w] > mx ? sel.tmp[w] : mx;
+            ish[0] = outk[K - 1] > mx ? 1 : 0;
+        }
+        sync();
+        merged = ish[0] != 0;
+        sync();
+    }
+    if (!merged) {
+        const int GK = G * K;
+        const int n = p.tp * GK;
+        auto cand_at = [&](int i) {
+            const int s = i / GK, r = i - s * GK;
+            return __ldcg(ck + s * sstride + (r / K) * kMaxTopK + (r % K));
+        };
+        if (static_cast<size_t>(n) * sizeof(uint64_t) > static_cast<size_t>(p.S) * kStageBytes) {  // ring too small
+            block_select_topk(n, K, cand_at, outk, sel, tid, kConsumerThreads, sync);
+        } else {
+            for (int i0 = 0; i0 < n; i0 += 16 * kConsumerThreads) {
+                uint64_t v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int i = i0 + tid + j * kConsumerThreads;
+                    v[j] = i < n ? cand_at(i) : 0ull;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int i = i0 + tid + j * kConsumerThreads;
+                    if (i < n) keys[i] = v[j];
+                }
+            }
+            sync();
+            block_select_topk(n, K, [&](int i) { return keys[i]; }, outk, sel, tid, kConsumerThreads, sync);
         }
     }
-    consumer_sync(kConsumerThreads);
-    block_select_topk(
-        n, K, [&](int i) { return keys[i]; }, outk, sel, tid, kConsumerThreads, [] { consumer_sync(kConsumerThreads); });
-    }
-    int32_t token = -1;
-    if (tid == 0 && ok) {
-        const double u = p.uniforms ? p.uniforms[b] : philox_uniform(p.seed, p.rng_offset, b);
-        token = draw_from_sorted(outk, K, p.temperature, p.top_p, u, fscr, oscr);
-    }
-    return token;
+    const double u = p.uniforms ? p.uniforms[b] : philox_uniform(p.seed, p.rng_offset, b);
+    const int32_t token = draw_block(outk, K, p.temperature, p.top_p, u, fscr, escr, oscr, ish, tid, kConsumerThreads,
+                                     sync);
+    return (tid == 0 && ok) ? token : -1;
 }
 
 // ---------------------------------------------------------------- consumer phases

@@ -475,8 +475,9 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         // then the P.V reduction block (1024 * Gq floats in the two-tile pass)
         xs = std::max(xs, (Gq + 2) * hd + Gq * 2 * kAttTile + 3 * kMaxQPerKv + 2 * hd + Bd * hd +
                               std::max(kConsumerThreads, 1024) * Gq + 8);
-        xs = std::max(xs, static_cast<int>((sizeof(uint32_t) * 264 + sizeof(uint64_t) * 1024 + kMaxTopK * 8 * 2 +
-                                            kMaxTopK * 4) / 4 + 16));
+        // selection and draw: SelectSmem, K keys, two double and one int scratch of K, 4 ints
+        xs = std::max(xs, static_cast<int>((sizeof(uint32_t) * 264 + sizeof(uint64_t) * 1024 + kMaxTopK * 8 * 3 +
+                                            kMaxTopK * 4 + 16) / 4 + 16));
         return (xs + 31) / 32 * 32;
     };
     m->S = 0;

@@ -51,9 +51,15 @@ __device__ uint64_t kth_key(int n, int K, KeyAt key_at, SampSmem &sm) {
     for (int shift = 56; shift >= 0; shift -= 8) {
         for (int i = tid; i < 256; i += kSampThreads) sm.sel.hist[i] = 0u;
         __syncthreads();
-        for (int i = tid; i < n; i += kSampThreads) {
-            const uint64_t k = key_at(i);
-            if ((k & mask) == prefix) atomicAdd(&sm.sel.hist[(k >> shift) & 255u], 1u);
+        for (int i0 = 0; i0 < n; i0 += kSampThreads) {  // warp-aggregated (see block_select_topk)
+            const int i = i0 + tid;
+            uint32_t dig = 256u;
+            if (i < n) {
+                const uint64_t k = key_at(i);
+                if ((k & mask) == prefix) dig = static_cast<uint32_t>((k >> shift) & 255u);
+            }
+            const uint32_t same = __match_any_sync(0xffffffffu, dig);
+            if (dig != 256u && (tid & 31) == __ffs(same) - 1) atomicAdd(&sm.sel.hist[dig], __popc(same));
         }
         __syncthreads();
         if (tid == 0) {

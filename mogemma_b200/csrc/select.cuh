@@ -82,9 +82,18 @@ __device__ void block_select_topk(int n, int K, KeyAt key_at, uint64_t *out, Sel
         for (int shift = 56; shift >= 0; shift -= 8) {
             for (int i = tid; i < 256; i += nthr) sm.hist[i] = 0u;
             sync();
-            for (int i = tid; i < n; i += nthr) {
-                const uint64_t k = key_at(i);
-                if ((k & mask) == prefix) atomicAdd(&sm.hist[(k >> shift) & 255u], 1u);
+            // Warp-aggregated histogram: lanes holding the same digit add once.
+            // Candidate keys of similar logits share their top digits, and plain
+            // per-key atomics on one bin serialise (tens of us for 9,472 keys).
+            for (int i0 = 0; i0 < n; i0 += nthr) {  // warp-uniform trip count
+                const int i = i0 + tid;
+                uint32_t dig = 256u;  // not in the current bucket
+                if (i < n) {
+                    const uint64_t k = key_at(i);
+                    if ((k & mask) == prefix) dig = static_cast<uint32_t>((k >> shift) & 255u);
+                }
+                const uint32_t same = __match_any_sync(0xffffffffu, dig);
+                if (dig != 256u && (tid & 31) == __ffs(same) - 1) atomicAdd(&sm.hist[dig], __popc(same));
             }
             sync();
             if (tid < 32) {
@@ -126,10 +135,20 @@ __device__ void block_select_topk(int n, int K, KeyAt key_at, uint64_t *out, Sel
         }
         if (tid == 0) sm.sh[3] = 0u;
         sync();
-        for (int i = tid; i < n; i += nthr) {
-            const uint64_t k = key_at(i);
-            if ((k & mask) >= prefix) {
-                const uint32_t slot = atomicAdd(&sm.sh[3], 1u);
+        for (int i0 = 0; i0 < n; i0 += nthr) {  // one slot reservation per warp
+            const int i = i0 + tid;
+            uint64_t k = 0;
+            bool take = false;
+            if (i < n) {
+                k = key_at(i);
+                take = (k & mask) >= prefix;
+            }
+            const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+            uint32_t base = 0;
+            if ((tid & 31) == 0 && ballot) base = atomicAdd(&sm.sh[3], static_cast<uint32_t>(__popc(ballot)));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (take) {
+                const uint32_t slot = base + static_cast<uint32_t>(__popc(ballot & ((1u << (tid & 31)) - 1u)));
                 if (slot < static_cast<uint32_t>(K)) sm.tmp[slot] = k;
             }
         }
@@ -201,6 +220,72 @@ __device__ inline int32_t draw_from_sorted(const uint64_t *keys, int n, double t
         if (cdf / total > u) return static_cast<int32_t>(key_index(keys[order[r]]));
     }
     return static_cast<int32_t>(key_index(keys[order[keep - 1]]));
+}
+
+// draw_from_sorted with its per-candidate float64 work spread over a thread
+// group: the divisions by the temperature, the exponentials and the index
+// ranks (the O(K^2) part) run one candidate per thread; the sums stay in one
+// thread, in the order of the serial rules, so every result is bit-identical
+// to draw_from_sorted.  All nthr threads call it; the token is valid in tid 0.
+// Scratch (shared memory): f, e [n] doubles, order [n] ints, sh [2] ints.
+template <class Sync>
+__device__ int32_t draw_block(const uint64_t *keys, int n, double temperature, double top_p, double u, double *f,
+                              double *e, int *order, int *sh, int tid, int nthr, Sync sync) {
+    if (temperature <= 0.0) return static_cast<int32_t>(key_index(keys[0]));
+    for (int i = tid; i < n; i += nthr) f[i] = static_cast<double>(key_value(keys[i])) / temperature;
+    sync();
+    const double fmax = f[0];
+    for (int i = tid; i < n; i += nthr) e[i] = exp(f[i] - fmax);
+    sync();
+    if (tid == 0) {
+        int nv = 0;
+        while (nv < n && key_index(keys[nv]) != 0xffffffffu) ++nv;
+        int keep = nv;
+        if (nv > 0 && isfinite(fmax) && top_p > 0.0 && top_p < 1.0) {
+            int nfin = 0;
+            while (nfin < nv && isfinite(f[nfin])) ++nfin;
+            double s = 0.0;
+            for (int i = 0; i < nfin; ++i) s += e[i];
+            double cum = 0.0;
+            for (int i = 0; i < nfin; ++i) {
+                cum += e[i] / s;
+                if (cum > top_p) {
+                    keep = i + 1;
+                    break;
+                }
+            }
+        }
+        sh[0] = nv;
+        sh[1] = keep;
+    }
+    sync();
+    const int nv = sh[0], keep = sh[1];
+    if (nv == 0) return 0;
+    if (!isfinite(fmax)) return static_cast<int32_t>(key_index(keys[0]));
+    for (int i = tid; i < keep; i += nthr) {
+        const uint32_t ii = key_index(keys[i]);
+        int r = 0;
+        for (int j = 0; j < keep; ++j) r += key_index(keys[j]) < ii;
+        order[r] = i;
+    }
+    sync();
+    int32_t token = -1;
+    if (tid == 0) {
+        double s2 = 0.0;
+        for (int i = 0; i < keep; ++i) s2 += e[i];
+        double total = 0.0;
+        for (int r = 0; r < keep; ++r) total += e[order[r]] / s2;
+        double cdf = 0.0;
+        token = static_cast<int32_t>(key_index(keys[order[keep - 1]]));
+        for (int r = 0; r < keep; ++r) {
+            cdf += e[order[r]] / s2;
+            if (cdf / total > u) {
+                token = static_cast<int32_t>(key_index(keys[order[r]]));
+                break;
+            }
+        }
+    }
+    return token;
 }
 
 }  // namespace mg
