@@ -393,6 +393,14 @@ def run_reference(args, world: int, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def metric_name(B: int, tp: int) -> str:
+    """METRIC for the default workload; the same wording with the batch, model and TP degree otherwise."""
+    m = METRIC if B == 1 else METRIC.replace("batch-1", f"batch-{B}")
+    if CONFIG != "gemma3-1b":
+        m = m.replace("Gemma3-1B", CONFIG.replace("gemma3", "Gemma3").replace("b", "B"))
+    return m if tp <= 1 else m.replace(") and", f", tensor-parallel x{tp}) and")
+
+
 def bench_config(world: int, B: int, tp: bool, weight_dtype: str = "f32") -> dict:
     """The workload description shared by the CUDA arm and the reference arm."""
     streams = 1 if tp else world
@@ -425,6 +433,11 @@ def main() -> None:
                     help="embed: sequences per step (the workload is 256; fewer for small profiling captures)")
     ap.add_argument("--parallel", default="replicas", choices=["replicas", "tp"],
                     help="N>1: independent replicas (weak scaling) or one tensor-parallel model over the N GPUs")
+    ap.add_argument("--device-weights", action="store_true",
+                    help="generate the seeded random weights on each GPU (Gemma3-4B/27B: larger than host memory)")
+    ap.add_argument("--mode", default="ref", choices=["ref", "gemma3"],
+                    help="gemma3: sliding window on 5 of 6 layers and dual RoPE theta (the 4B/27B configurations)")
+    ap.add_argument("--e2e-passes", type=int, default=10, help="decode passes timed end to end (at least)")
     args = ap.parse_args()
     CONFIG, PROMPT, DECODE = args.model, args.prompt, args.decode
     world, rank, local = dist_setup()
@@ -445,15 +458,25 @@ def main() -> None:
     from mogemma_b200 import _core, synth  # noqa: PLC0415
 
     d = synth.CONFIGS[CONFIG]
-    weights = synth.make_weights(d, seed=0, bf16=args.weight_dtype == "bf16")
     tp = args.parallel == "tp" and world > 1
     B = args.batch
     opts = dict(device=local, capacity=PROMPT + DECODE, max_batch=B, weight_dtype=args.weight_dtype,
-                prefill_path=1 if B > 1 else 0)
-    if tp:  # every rank holds its shard; the same seed on every rank draws the same tokens
-        llm = _core.init_model_tp(synth.metadata_of(weights), seed=1234, **opts)
+                prefill_path=1 if B > 1 and not tp else 0)
+    if args.device_weights:
+        # seeded N(0, 0.02) weights generated on each device (models larger than host memory);
+        # every rank generates the same full tensors and keeps its shard
+        meta = {k: (0, v, "F32") for k, v in synth.tensor_shapes(d).items()}
+        meta["lm_head.weight"] = (0, (d.vocab, d.hidden), "F32")
+        opts.update(synthetic_std=0.02, synthetic_seed=1)
     else:
-        llm = _core.init_model(synth.metadata_of(weights), seed=1234 + rank, **opts)
+        weights = synth.make_weights(d, seed=0, bf16=args.weight_dtype == "bf16")
+        meta = synth.metadata_of(weights)
+    if args.mode == "gemma3":
+        opts.update(mode="gemma3", sliding_window=d.window, global_every=6)
+    if tp:  # every rank holds its shard; the same seed on every rank draws the same tokens
+        llm = _core.init_model_tp(meta, seed=1234, **opts)
+    else:
+        llm = _core.init_model(meta, seed=1234 + rank, **opts)
     h = llm["_handle"]
     info = h.info
     lib = _core.lib()
@@ -512,18 +535,18 @@ def main() -> None:
     e2e_step()
     barrier(world)
     t0 = time.perf_counter()
-    e2e_steps = max(10, args.steps)
+    e2e_steps = max(args.e2e_passes, args.steps)
     for _ in range(e2e_steps):
         e2e_step()
     e2e_s = dist_max(time.perf_counter() - t0, world)
     e2e_value = e2e_steps * DECODE * streams * B / e2e_s
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.device_weights:
         cpu = cpu_baseline(weights, 1, args.cpu_sample)
     if rank == 0:
         line = {
-            "metric": METRIC if B == 1 else METRIC.replace("batch-1", f"batch-{B}"), "value": value, "unit": UNIT,
+            "metric": metric_name(B, world if tp else 1), "value": value, "unit": UNIT,
             "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if tp else "weak",

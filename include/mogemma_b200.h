@@ -88,6 +88,15 @@ typedef struct mg_options {
                                  reference's arithmetic); 1: all prompt tokens per layer at once, projections
                                  as tcgen05 GEMMs on bf16-rounded inputs (tp_size 1) */
     const void *reserved1;
+    /* Device-generated weights, for benchmarks of models larger than host memory
+     * (no counterpart in the reference, which reads every tensor from its
+     * checkpoint): when synthetic_std > 0, every tensor whose data pointer is NULL
+     * is filled on the device with N(0, synthetic_std) values from a counter-based
+     * generator keyed by (synthetic_seed, tensor name, element index); lm_head.weight
+     * uses the embedding's key (tied).  Read only when struct_size covers them. */
+    float synthetic_std;
+    int32_t reserved2;
+    uint64_t synthetic_seed;
 } mg_options;
 
 typedef struct mg_model_info {
@@ -192,6 +201,17 @@ mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const int32_t *le
  * the attention from the cache): treat its decode state as lost. */
 mg_status mg_encode(mg_model *m, const int32_t *token_ids_host, const int32_t *lens_host, int32_t batch,
                     int32_t max_len, float *out_host);
+
+/* ---- failure-detection test hooks (no counterpart in the reference, whose
+ * engine has no device waits) ----
+ * wait_budget_ns: budget of every bounded wait of the decode kernel (0: the
+ * default of 2 s).  stall_phase: a phase whose outputs one CTA withholds (-1:
+ * none; phase 5 * layer + {0 QKV, 1 attention, 2 o_proj, 3 gate/up, 4 down},
+ * 5 * layers the lm_head): the waits on them run out, the kernel records the
+ * site, fast-forwards to its end, and the call returns MG_ERR_TIMEOUT with the
+ * model's positions restored and the model usable.  Production callers leave
+ * both unset. */
+mg_status mg_set_debug(mg_model *m, uint64_t wait_budget_ns, int32_t stall_phase);
 
 /* ---- inspection (tests) ---- */
 mg_status mg_read_kv(const mg_model *m, int32_t layer, int32_t row, int32_t pos, float *k_host, float *v_host);

@@ -78,6 +78,9 @@ class Options(ctypes.Structure):
         ("tp_size", ctypes.c_int32),
         ("prefill_path", ctypes.c_int32),
         ("reserved1", ctypes.c_void_p),
+        ("synthetic_std", ctypes.c_float),
+        ("reserved2", ctypes.c_int32),
+        ("synthetic_seed", ctypes.c_uint64),
     ]
 
 
@@ -133,9 +136,11 @@ _lib.mg_tp_disconnect.argtypes = [_P]
 TP_HANDLE_BYTES = 64  # MG_TP_HANDLE_BYTES
 _lib.mg_trace_enable.argtypes = [_P, ctypes.c_int32]
 _lib.mg_trace_read.argtypes = [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)]
+_lib.mg_set_debug.argtypes = [_P, ctypes.c_uint64, ctypes.c_int32]
 for _f in ("mg_model_create", "mg_model_info_get", "mg_model_destroy", "mg_set_pos", "mg_get_pos", "mg_step",
            "mg_prefill", "mg_generate", "mg_set_tokens", "mg_sample", "mg_embed", "mg_read_kv",
-           "mg_tp_ipc_handle", "mg_tp_connect", "mg_tp_disconnect", "mg_encode", "mg_trace_enable", "mg_trace_read"):
+           "mg_tp_ipc_handle", "mg_tp_connect", "mg_tp_disconnect", "mg_encode", "mg_trace_enable", "mg_trace_read",
+           "mg_set_debug"):
     getattr(_lib, _f).restype = ctypes.c_int
 
 
@@ -191,6 +196,10 @@ class ModelHandle:
         _check(_lib.mg_set_pos(self.ptr, row, int(pos)))
         if row in (-1, 0):
             self.pos = int(pos)
+
+    def set_debug(self, wait_budget_ns: int = 0, stall_phase: int = -1) -> None:
+        """Failure-detection test hook: wait budget of the decode kernel and a phase whose outputs are withheld."""
+        _check(_lib.mg_set_debug(self.ptr, int(wait_budget_ns), int(stall_phase)))
 
     def trace(self, on: bool = True) -> None:
         """Record a per-CTA, per-phase timeline of every decode launch."""
@@ -280,6 +289,8 @@ def create_model(metadata: dict[str, Any], **options: Any) -> ModelHandle:
     o.stream = options.get("stream")
     o.decode_path = int(options.get("decode_path", _env_int("MOGEMMA_B200_DECODE_PATH", 0)))
     o.prefill_path = int(options.get("prefill_path", _env_int("MOGEMMA_B200_PREFILL", 0)))
+    o.synthetic_std = float(options.get("synthetic_std", 0.0))
+    o.synthetic_seed = int(options.get("synthetic_seed", 0)) & 0xFFFFFFFFFFFFFFFF
     o.tp_rank = int(options.get("tp_rank", 0))
     o.tp_size = int(options.get("tp_size", 1))
     out = _P()

@@ -88,7 +88,8 @@ __device__ __forceinline__ void tg_load2(const uint64_t *p, uint64_t &a, uint64_
 // until all do.  Bounded like every wait here: false after the budget or once
 // another thread has recorded an error (then the values are not to be used).
 template <int N, typename Src>
-__device__ __forceinline__ bool tg_settle(uint64_t (&w)[N], uint32_t tag, Src src, uint32_t *err, uint32_t site) {
+__device__ __forceinline__ bool tg_settle(uint64_t (&w)[N], uint32_t tag, Src src, uint32_t *err, uint32_t site,
+                                          uint64_t budget = kWaitBudgetNs) {
     auto all = [&]() {
         bool a = true;
 #pragma unroll
@@ -104,7 +105,7 @@ __device__ __forceinline__ bool tg_settle(uint64_t (&w)[N], uint32_t tag, Src sr
         if (all()) return true;
         if ((n & 7u) == 0u) {
             if (ld_relaxed_u32(err) != 0u) return false;
-            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            if (globaltimer_ns() - t0 > budget) {
                 set_error(err, kErrTimeoutCounter | site);
                 return false;
             }
@@ -114,7 +115,7 @@ __device__ __forceinline__ bool tg_settle(uint64_t (&w)[N], uint32_t tag, Src sr
 
 // Wait until *ctr >= target (acquire).  Returns false on error/timeout.
 __device__ __forceinline__ bool wait_counter_geq(const uint32_t *ctr, uint32_t target, uint32_t *err,
-                                                 uint32_t site) {
+                                                 uint32_t site, uint64_t budget = kWaitBudgetNs) {
     if (ld_acquire_u32(ctr) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t n = 1;; ++n) {
@@ -123,7 +124,7 @@ __device__ __forceinline__ bool wait_counter_geq(const uint32_t *ctr, uint32_t t
         // is another dependent round trip between two polls
         if ((n & 7u) == 0u) {
             if (ld_relaxed_u32(err) != 0u) return false;
-            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            if (globaltimer_ns() - t0 > budget) {
                 set_error(err, kErrTimeoutCounter | site);
                 return false;
             }
@@ -134,14 +135,14 @@ __device__ __forceinline__ bool wait_counter_geq(const uint32_t *ctr, uint32_t t
 // Wait until the 64-bit counter *ctr (incremented by this and peer GPUs)
 // reaches target (acquire at system scope).  Returns false on error/timeout.
 __device__ __forceinline__ bool wait_counter_geq_sys(const uint64_t *ctr, uint64_t target, uint32_t *err,
-                                                     uint32_t site) {
+                                                     uint32_t site, uint64_t budget = kWaitBudgetNs) {
     if (ld_acquire_sys_u64(ctr) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t n = 1;; ++n) {
         if (ld_acquire_sys_u64(ctr) >= target) return true;
         if ((n & 7u) == 0u) {
             if (ld_relaxed_u32(err) != 0u) return false;
-            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            if (globaltimer_ns() - t0 > budget) {
                 set_error(err, kErrTimeoutCounter | site);
                 return false;
             }
@@ -206,14 +207,15 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
 constexpr uint32_t kMbarSleepNs = 20000;  // longest sleep per poll; a completed phase wakes the thread
 // Bounded wait for the phase with `parity` to complete.  The error word and
 // the clock are consulted only every 32 polls, keeping the hot poll local.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code,
+                                          uint64_t budget = kWaitBudgetNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t n = 1;; ++n) {
         if (mbar_try_wait_sleep(bar, parity, kMbarSleepNs)) return true;
         if ((n & 31u) == 0u) {
             if (ld_relaxed_u32(err) != 0u) return false;
-            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            if (globaltimer_ns() - t0 > budget) {
                 set_error(err, code);
                 return false;
             }

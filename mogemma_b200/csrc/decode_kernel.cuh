@@ -39,6 +39,10 @@
 
 namespace mg {
 
+// The launch's budget for every bounded wait (ns of %globaltimer), set by thread
+// 0 from DecodeParams::wait_ns before the first wait.
+__shared__ uint64_t g_wait_ns;
+
 // ---------------------------------------------------------------- sync layout
 __device__ __forceinline__ uint32_t *ctr_phase(const DecodeParams &p, int ph) { return p.sync + ph; }
 __device__ __forceinline__ uint32_t *ctr_exit(const DecodeParams &p) { return p.sync + p.n_phases; }
@@ -290,10 +294,10 @@ __device__ __forceinline__ bool stage_norm(const uint64_t *base, const uint64_t 
                 }
             }
             auto bsrc = [&](int j) { return brow + tid + (j0 + j) * kConsumerThreads; };
-            ok = tg_settle(wb, tag, bsrc, err, site) && ok;
+            ok = tg_settle(wb, tag, bsrc, err, site, g_wait_ns) && ok;
             if constexpr (!XSUM) {
                 auto asrc = [&](int j) { return arow + tid + (j0 + j) * kConsumerThreads; };
-                ok = tg_settle(wa, tag, asrc, err, site) && ok;
+                ok = tg_settle(wa, tag, asrc, err, site, g_wait_ns) && ok;
 #pragma unroll
                 for (int j = 0; j < kNormPer; ++j) v[j] = tg_val(wa[j]);
             }
@@ -415,7 +419,7 @@ __device__ __forceinline__ void phase_done(SmallSmem &ss, int tid) {
 __device__ __forceinline__ bool cta_wait(const uint32_t *ctr, uint32_t target, uint32_t *err, uint32_t site,
                                          SmallSmem &ss, int tid) {
     if (tid == 0) {
-        ss.flag = wait_counter_geq(ctr, target, err, site) ? 1u : 0u;
+        ss.flag = wait_counter_geq(ctr, target, err, site, g_wait_ns) ? 1u : 0u;
         trace_mark(ss.tr_ready);
     }
     consumer_sync(kConsumerThreads);
@@ -446,7 +450,7 @@ __device__ __forceinline__ bool xwait(const DecodeParams &p, int which, uint64_t
                                       SmallSmem &ss, int tid) {
     if (tid == 0) {
         const uint64_t target = (index + 1) * static_cast<uint64_t>(p.tp) * gridDim.x;
-        ss.flag = wait_counter_geq_sys(xcnt(p, p.tp_rank, which), target, p.err, site) ? 1u : 0u;
+        ss.flag = wait_counter_geq_sys(xcnt(p, p.tp_rank, which), target, p.err, site, g_wait_ns) ? 1u : 0u;
         trace_mark(ss.tr_ready);
     }
     consumer_sync(kConsumerThreads);
@@ -469,6 +473,7 @@ struct GemvOut {
     uint32_t tag;
     float *const *xdst = nullptr;
     int nx = 0;
+    bool mute = false;  // test hook (DecodeParams::stall_phase): the results are withheld
 };
 __device__ __forceinline__ GemvOut gemv_out_tagged(uint64_t *out, int64_t ld, uint32_t tag) {
     return GemvOut{out, nullptr, ld, tag};
@@ -478,6 +483,7 @@ __device__ __forceinline__ GemvOut gemv_out_peers(float *const *xdst, int nx, in
     return GemvOut{nullptr, nullptr, ld, 0u, xdst, nx};
 }
 __device__ __forceinline__ void gemv_store(const GemvOut &o, int64_t idx, float v) {
+    if (o.mute) return;
     if (o.nx) {
         for (int k = 0; k < o.nx; ++k) o.xdst[k][idx] = v;
     } else if (o.tout) {
@@ -507,7 +513,7 @@ __device__ __forceinline__ void gemv_tiles(const GemvGeom<WT> &g, const float *_
         for (int s = 0; s < g.nseg; ++s, ++tile) {
             const int st = static_cast<int>(tile % S);
             const uint32_t par = (tile / S) & 1u;
-            if (ok) ok = mbar_wait(&sm.full[st], par, err, kErrTimeoutFull | 1u);
+            if (ok) ok = mbar_wait(&sm.full[st], par, err, kErrTimeoutFull | 1u, g_wait_ns);
             if (grp == 0 && s == 0 && tid == 0) trace_mark(tr_first);
             const int c0 = s * g.kc;
             const int sw = min(g.kc, Kp - c0);
@@ -651,7 +657,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
             uint64_t w[kPer];
 #pragma unroll
             for (int j = 0; j < kPer; ++j) w[j] = tid + j * kConsumerThreads < n ? tg_load(src(j)) : tg_pack(0.f, tag);
-            ok = tg_settle(w, tag, src, p.err, 100 + ph) && ok;
+            ok = tg_settle(w, tag, src, p.err, 100 + ph, g_wait_ns) && ok;
 #pragma unroll
             for (int j = 0; j < kPer; ++j) {
                 const int i = tid + j * kConsumerThreads;
@@ -736,7 +742,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
                 for (int u = 0; u < 2; ++u) {
                     const uint32_t tu = tile + static_cast<uint32_t>(min(u, ntl - 1));
                     const int st = static_cast<int>(tu % p.S);
-                    if (u < ntl && ok) ok = mbar_wait(&sm.full[st], (tu / p.S) & 1u, p.err, kErrTimeoutFull | 2u);
+                    if (u < ntl && ok) ok = mbar_wait(&sm.full[st], (tu / p.S) & 1u, p.err, kErrTimeoutFull | 2u, g_wait_ns);
                     kt[u] = reinterpret_cast<const float *>(sm.ring + static_cast<size_t>(st) * kStageBytes);
                     vt[u] = kt[u] + kAttTile * HD;
                 }
@@ -850,7 +856,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
         for (int h = 0; h < kQ; ++h) acc[h] = 0.f;
         for (int ts = t_begin; ts < t_end; ts += kAttTile, ++tile) {
             const int st = static_cast<int>(tile % p.S);
-            if (ok) ok = mbar_wait(&sm.full[st], (tile / p.S) & 1u, p.err, kErrTimeoutFull | 2u);
+            if (ok) ok = mbar_wait(&sm.full[st], (tile / p.S) & 1u, p.err, kErrTimeoutFull | 2u, g_wait_ns);
             if (tid == 0 && done == 0 && ts == t_begin) trace_mark(trace_slot(p, ph, kTrPrologue));
             const int nt = min(kAttTile, t_end - ts);
             const float *kt = reinterpret_cast<const float *>(sm.ring + static_cast<size_t>(st) * kStageBytes);
@@ -1244,6 +1250,13 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
         phase_of(ph, p.L, kind, layer);
         const LayerPtrs &lp = sm.layers[layer];
         const bool has_dep = ph - 1 >= p.ph_begin;
+        // test hook: one CTA with work in this phase withholds its outputs (the last
+        // slot always owns rows of a projection; slot 0 owns attention item 0)
+        const bool mute = ph == p.stall_phase && cta_slot(ph) == (kind == PH_ATT ? 0 : G - 1);
+        auto muted = [mute](GemvOut o) {
+            o.mute = mute;
+            return o;
+        };
         if (tid == 0) {
             trace_mark(trace_slot(p, ph, kTrStart));
             ss.tr_ready = trace_slot(p, ph, kTrReady);
@@ -1274,7 +1287,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             }
             if (tid == 0) trace_mark(ss.tr_ready);
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                                 gemv_out_tagged(p.qkv, p.qkv_rows, tag));
+                                 muted(gemv_out_tagged(p.qkv, p.qkv_rows, tag)));
             phase_done(ss, tid);
         } else if (kind == PH_ATT) {
             if (tid == 0) att_rows<NB>(p, lp.is_global != 0, ss.pos, ss.att);
@@ -1282,7 +1295,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             const AttRet r = att_dispatch(p, sm, ss, lp, layer, ph, ss.att, tile, ok, tid, has_dep);
             tile = r.tile;
             ok = r.ok;
-            cta_signal(ctr_phase(p, ph), r.done, ss, tid);
+            cta_signal(ctr_phase(p, ph), mute ? 0u : r.done, ss, tid);
         } else if (kind == PH_O) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
@@ -1295,7 +1308,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             att_combine(p, ss.att, g.Kp, sm.xs, tid);
             // with tensor parallelism the row-split o_proj partials go to every rank
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                                 TP ? gemv_out_peers(ss.xdst_o, p.tp, p.H) : gemv_out_tagged(p.o_raw, p.H, tag));
+                                 muted(TP ? gemv_out_peers(ss.xdst_o, p.tp, p.H) : gemv_out_tagged(p.o_raw, p.H, tag)));
             phase_done(ss, tid);
             if constexpr (TP) xsignal(p, 0, tid);
         } else if (kind == PH_GU) {
@@ -1317,8 +1330,8 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             }
             if (tid == 0) trace_mark(ss.tr_ready);
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                                 gemv_out_float(p.act, p.Ip));
-            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+                                 muted(gemv_out_float(p.act, p.Ip)));
+            cta_signal(ctr_phase(p, ph), mute ? 0u : 1u, ss, tid);
         } else if (kind == PH_D) {
             GemvGeom<WT> g;
             gemv_geom<WT>(p, lp, kind, ph, g);
@@ -1343,7 +1356,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             }
             consumer_sync(kConsumerThreads);
             gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                                 TP ? gemv_out_peers(ss.xdst_d, p.tp, p.H) : gemv_out_tagged(p.mlp_raw, p.H, tag));
+                                 muted(TP ? gemv_out_peers(ss.xdst_d, p.tp, p.H) : gemv_out_tagged(p.mlp_raw, p.H, tag)));
             phase_done(ss, tid);
             if constexpr (TP) xsignal(p, 1, tid);
         } else if (kind == PH_LMH) {
@@ -1372,13 +1385,13 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                                 p.emb_acc[static_cast<int64_t>(b) * p.H + i] += sm.xs[b * g.Kp + i];
             } else if (p.lm_mode == kLmLogits) {
                 gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
-                                     gemv_out_float(p.logits, p.V));
+                                     muted(gemv_out_float(p.logits, p.V)));
                 if (p.topk > 0) {
                     consumer_sync(kConsumerThreads);
                     lm_topk(p, sm, g.row0, g.nrows, tid);
                 }
             }
-            cta_signal(ctr_phase(p, ph), 1u, ss, tid);
+            cta_signal(ctr_phase(p, ph), mute ? 0u : 1u, ss, tid);
             // every rank's logits and candidates are complete once this exchange is counted
             if constexpr (TP)
                 if (p.lm_mode == kLmLogits) xsignal(p, 2, tid);
@@ -1417,10 +1430,10 @@ __device__ void producer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
     // Slot for tile t: its stage was released by the consumers (tile t - S), and
     // at most `inflight` copies are outstanding (tile t - inflight has landed).
     auto acquire_slot = [&](uint32_t t) -> bool {
-        if (t >= S && !mbar_wait(&sm.empty[t % S], ((t / S) - 1) & 1u, p.err, kErrTimeoutEmpty | 1u)) return false;
+        if (t >= S && !mbar_wait(&sm.empty[t % S], ((t / S) - 1) & 1u, p.err, kErrTimeoutEmpty | 1u, g_wait_ns)) return false;
         if (t >= inflight) {
             const uint32_t u = t - inflight;
-            if (u < issued && !mbar_wait(&sm.full[u % S], (u / S) & 1u, p.err, kErrTimeoutFull | 3u)) return false;
+            if (u < issued && !mbar_wait(&sm.full[u % S], (u / S) & 1u, p.err, kErrTimeoutFull | 3u, g_wait_ns)) return false;
         }
         return true;
     };
@@ -1514,7 +1527,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         sl.empty = sl.full + p.S;
         sl.layers = reinterpret_cast<LayerPtrs *>(sl.empty + p.S);
     }
-    if (threadIdx.x == 0) sm = sl;
+    if (threadIdx.x == 0) {
+        sm = sl;
+        g_wait_ns = p.wait_ns ? p.wait_ns : kWaitBudgetNs;
+    }
     const int tid = threadIdx.x;
     const int G = gridDim.x;
 

@@ -34,6 +34,8 @@ cudaError_t sample_rows_launch(const float *logits, int64_t ld, int rows, int V,
                                int32_t *tok, cudaStream_t stream);
 cudaError_t convert_rows_launch(const void *src, int src_dtype, int64_t rows, int64_t cols, void *dst, int dst_dtype,
                                 int64_t dst_ld, cudaStream_t stream);
+cudaError_t synth_fill_launch(float *dst, int64_t rows, int64_t cols, int64_t row0, int64_t col0, int64_t full_cols,
+                              uint64_t key, float std, cudaStream_t stream);
 cudaError_t gemm_bf16_tc(const void *A, int64_t lda, const void *B, int64_t ldb, float *C, int64_t ldc, int M, int N,
                          int K, uint32_t *err, cudaStream_t stream, float *ws, size_t ws_floats);
 cudaError_t pf_advance(int32_t *pos, int n, cudaStream_t s);
@@ -142,6 +144,8 @@ struct mg_model {
     int32_t *pinned = nullptr;  // pinned staging for small transfers
     uint64_t *trace = nullptr;  // decode timeline (mg_trace_enable)
     bool trace_on = false;
+    uint64_t wait_ns = 0;       // decode-kernel wait budget (0: the default 2 s); mg_set_debug
+    int stall_phase = -1;       // test hook: phase whose outputs CTA 0 withholds; mg_set_debug
     int max_inflight = 2;       // outstanding bulk copies per CTA (MOGEMMA_B200_INFLIGHT)
     int pf_tiles = 0;           // L2 prefetch distance in tiles (MOGEMMA_B200_PREFETCH)
 
@@ -231,6 +235,12 @@ struct Desc {
     std::vector<int64_t> shape;
     int dtype = MG_F32;
     int64_t ld = 0;  // host row stride in elements (0: the tensor's own width)
+    // device-generated tensor (data == nullptr, mg_options.synthetic_std > 0):
+    // generator key, std, and the view's first row / column in the full tensor
+    bool synthetic = false;
+    uint64_t key = 0;
+    float std = 0.f;
+    int64_t row0 = 0, col0 = 0;
 };
 
 // Rows [row0, ...) of a [rows, cols] tensor, and columns [col0, ...) (a strided
@@ -238,6 +248,10 @@ struct Desc {
 // shard through these.
 static Desc rows_view(const Desc &d, int64_t row0) {
     Desc v = d;
+    if (d.synthetic) {
+        v.row0 += row0;
+        return v;
+    }
     const int64_t w = d.ld ? d.ld : (d.shape.size() > 1 ? d.shape[1] : 1);
     v.data = static_cast<const char *>(d.data) + row0 * w * static_cast<int64_t>(dsize(d.dtype));
     return v;
@@ -245,12 +259,22 @@ static Desc rows_view(const Desc &d, int64_t row0) {
 static Desc cols_view(const Desc &d, int64_t col0) {
     Desc v = d;
     v.ld = d.ld ? d.ld : d.shape[1];
+    if (d.synthetic) {
+        v.col0 += col0;
+        return v;
+    }
     v.data = static_cast<const char *>(d.data) + col0 * static_cast<int64_t>(dsize(d.dtype));
     return v;
 }
 
-// Host rows [r0, r0 + nr) of d (width cols) into contiguous staging memory.
+// Host rows [r0, r0 + nr) of d (width cols) into contiguous staging memory
+// (generated there for a synthetic tensor).
 static cudaError_t stage_rows(mg_model *m, const Desc &d, int64_t r0, int64_t nr, int64_t cols, void *staging) {
+    if (d.synthetic) {
+        const int64_t full = d.shape.size() > 1 ? d.shape[1] : (d.shape.empty() ? 1 : d.shape[0]);
+        return synth_fill_launch(static_cast<float *>(staging), nr, cols, d.row0 + r0, d.col0, full, d.key, d.std,
+                                 m->stream);
+    }
     const size_t es = dsize(d.dtype);
     const int64_t w = d.ld ? d.ld : cols;
     const char *src = static_cast<const char *>(d.data) + r0 * w * static_cast<int64_t>(es);
@@ -316,12 +340,28 @@ extern "C" void *mg_model_stream(const mg_model *m) { return m ? static_cast<voi
 
 static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_options *opt, mg_model *m) {
     std::map<std::string, Desc> d;
+    const bool has_syn = opt && opt->struct_size >= static_cast<int32_t>(offsetof(mg_options, synthetic_seed) +
+                                                                         sizeof(uint64_t));
+    const float syn_std = has_syn ? opt->synthetic_std : 0.f;
     for (int i = 0; i < n; ++i) {
         if (!descs[i].name) return fail(MG_ERR_INVALID, "tensor %d has no name", i);
         Desc x;
         x.data = descs[i].data;
         x.dtype = descs[i].dtype;
         for (int k = 0; k < descs[i].ndim && k < 4; ++k) x.shape.push_back(descs[i].shape[k]);
+        if (!x.data) {
+            if (!(syn_std > 0.f))
+                return fail(MG_ERR_INVALID, "tensor '%s' has no data (synthetic weights need synthetic_std > 0)",
+                            descs[i].name);
+            std::string keyname = descs[i].name;
+            if (keyname == "lm_head.weight") keyname = "model.embed_tokens.weight";  // tied
+            uint64_t h = 1469598103934665603ull ^ opt->synthetic_seed;  // FNV-1a of the name
+            for (char ch : keyname) h = (h ^ static_cast<unsigned char>(ch)) * 1099511628211ull;
+            x.synthetic = true;
+            x.key = h;
+            x.std = syn_std;
+            x.dtype = MG_F32;  // generated as F32 in the staging buffer
+        }
         d[descs[i].name] = x;
     }
     m->dev = opt ? opt->device : 0;
@@ -397,7 +437,7 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         if (r0 != r || (c != 0 && c0 != c))
             return fail(MG_ERR_INVALID, "tensor %s has shape (%lld, %lld), expected (%lld, %lld)", nm.c_str(),
                         (long long)r0, (long long)c0, (long long)r, (long long)c);
-        if (!x->data) return fail(MG_ERR_INVALID, "tensor %s has a null data pointer", nm.c_str());
+        if (!x->data && !x->synthetic) return fail(MG_ERR_INVALID, "tensor %s has a null data pointer", nm.c_str());
         return MG_OK;
     };
     TRY(need(emb, m->V, m->H, "model.embed_tokens.weight"));
@@ -829,6 +869,8 @@ static DecodeParams base_params(mg_model *m, int B) {
     p.sync = m->sync;
     p.err = m->err;
     p.max_inflight = m->max_inflight;
+    p.wait_ns = m->wait_ns;
+    p.stall_phase = m->stall_phase;
     p.pf_tiles = m->pf_tiles;
     p.trace = m->trace_on ? m->trace : nullptr;
     p.n_phases = num_phases(m->L);
@@ -1441,6 +1483,15 @@ extern "C" mg_status mg_embed(mg_model *m, const int32_t *token_ids_host, const 
     }
     m->h_pos = pos_saved;
     CU(cudaMemcpy(m->pos, m->h_pos.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice));
+    return MG_OK;
+}
+
+extern "C" mg_status mg_set_debug(mg_model *m, uint64_t wait_budget_ns, int32_t stall_phase) {
+    if (!m) return fail(MG_ERR_INVALID, "null model");
+    if (stall_phase < -1 || stall_phase >= num_phases(m->L))
+        return fail(MG_ERR_INVALID, "stall_phase %d outside [-1, %d)", stall_phase, num_phases(m->L));
+    m->wait_ns = wait_budget_ns;
+    m->stall_phase = stall_phase;
     return MG_OK;
 }
 

@@ -39,9 +39,9 @@ def test_struct_layout_matches_header(tmp_path: Path) -> None:
     src = tmp_path / "sizes.c"
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "mogemma_b200.h"\n'
-        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(mg_tensor_desc), sizeof(mg_options),"
+        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(mg_tensor_desc), sizeof(mg_options),"
         " sizeof(mg_model_info), sizeof(mg_sampling), offsetof(mg_options, seed), offsetof(mg_options, reserved1),"
-        " offsetof(mg_sampling, uniforms_host)); return 0;}\n")
+        " offsetof(mg_sampling, uniforms_host), offsetof(mg_options, synthetic_seed)); return 0;}\n")
     exe = tmp_path / "sizes"
     try:
         subprocess.run(["gcc", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
@@ -52,7 +52,7 @@ def test_struct_layout_matches_header(tmp_path: Path) -> None:
 
     want = [ctypes.sizeof(_core.TensorDesc), ctypes.sizeof(_core.Options), ctypes.sizeof(_core.ModelInfo),
             ctypes.sizeof(_core.Sampling), _core.Options.seed.offset, _core.Options.reserved1.offset,
-            _core.Sampling.uniforms_host.offset]
+            _core.Sampling.uniforms_host.offset, _core.Options.synthetic_seed.offset]
     assert got == want
 
 
