@@ -38,16 +38,29 @@ def _free_port() -> int:
         return int(s.getsockname()[1])
 
 
-@pytest.mark.parametrize("kv_heads", [1, 2])
-def test_tensor_parallel_decode_matches_oracle(tmp_path: Path, kv_heads: int) -> None:
-    if _gpus() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run(tmp_path: Path, ranks: int, kv_heads: int, heads: int = 4, head_dim: int = 64) -> None:
     out = tmp_path / "tp.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={ranks}",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(ROOT / "tests" / "tp_worker.py"),
-           "--out", str(out), "--kv-heads", str(kv_heads)]
+           "--out", str(out), "--kv-heads", str(kv_heads), "--heads", str(heads), "--head-dim", str(head_dim)]
     proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600, check=False)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
     res = json.loads(out.read_text())
     assert res["ok"], res
+
+
+@pytest.mark.parametrize("kv_heads", [1, 2])
+def test_tensor_parallel_decode_matches_oracle(tmp_path: Path, kv_heads: int) -> None:
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run(tmp_path, 2, kv_heads)
+
+
+@pytest.mark.parametrize("ranks", [4, 8])
+def test_tensor_parallel_27b_head_geometry(tmp_path: Path, ranks: int) -> None:
+    """Gemma3-27B's head geometry (head dim 128, 2 q heads per kv head: 16 q / 8 kv heads here) split over 4
+    and 8 ranks: every rank keeps 2 or 1 kv heads with their q heads."""
+    if _gpus() < ranks:
+        pytest.skip(f"needs {ranks} GPUs")
+    _run(tmp_path, ranks, kv_heads=8, heads=16, head_dim=128)

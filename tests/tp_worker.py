@@ -32,6 +32,8 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--kv-heads", type=int, default=1)
+    ap.add_argument("--heads", type=int, default=4)
+    ap.add_argument("--head-dim", type=int, default=64)
     ap.add_argument("--steps", type=int, default=12)
     args = ap.parse_args()
 
@@ -44,12 +46,12 @@ def main() -> int:
     world = int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
-    d = synth.tiny(heads=4, kv_heads=args.kv_heads, intermediate=512, vocab=4096)
+    d = synth.tiny(heads=args.heads, kv_heads=args.kv_heads, head_dim=args.head_dim, intermediate=512, vocab=4096)
     w = synth.make_weights(d, seed=11)
     meta = synth.metadata_of(w)
     llm = _core.init_model_tp(meta, device=rank, capacity=64, seed=7)
     toks = [int(t) for t in synth.prompt_ids(args.steps, d.vocab, seed=5)]
-    result: dict = {"world": world, "kv_heads": args.kv_heads}
+    result: dict = {"world": world, "kv_heads": args.kv_heads, "heads": args.heads, "head_dim": args.head_dim}
 
     def run(model: dict) -> tuple[list, list, list]:
         # teacher-forced logits (the reference step(): full-vocabulary fp32 logits),
