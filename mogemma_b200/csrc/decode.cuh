@@ -106,7 +106,7 @@ struct DecodeParams {
     uint32_t pad4_;
     uint64_t wait_ns;     // budget of every bounded wait (0: the default, kWaitBudgetNs)
     int32_t stall_phase;  // test hook: one CTA withholds its outputs of this phase (-1: none)
-    int32_t pad5_;
+    int32_t att_split;    // 1: attention items per q head (head dim 256 only); 0: per kv head group
     uint32_t *sync;   // phase counters [n_phases], att_done [L], att_cnt [B*Hkv], exit [1]
     uint32_t *err;    // device error word
     int32_t n_phases;

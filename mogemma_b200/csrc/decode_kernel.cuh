@@ -124,7 +124,10 @@ __device__ __forceinline__ void gemv_geom(const DecodeParams &p, const LayerPtrs
     g.tiles = base + static_cast<int64_t>(g0) * g.nseg * g.tile_elems;
 }
 
-// Attention work split: items are (row, kv head, chunk of att_ch positions).
+// Attention work split: items are (row, unit, chunk of att_ch positions), a
+// unit being a kv head with its q heads, or (att_split) a single q head --
+// four times the items for Gemma3-1B's 4 q heads per kv head, each a quarter
+// of the work, so the phase ends sooner when CTAs are idle anyway.
 struct AttRows {
     int lo[kMaxRows], nch[kMaxRows];
     int nitems;
@@ -141,23 +144,29 @@ __device__ __forceinline__ void att_rows(const DecodeParams &p, bool global, con
             if (!global && p.window > 0 && pos - p.window + 1 > 0) lo = pos - p.window + 1;
             a.lo[b] = lo;
             a.nch[b] = (pos + 1 - lo + p.att_ch - 1) / p.att_ch;
-            a.nitems += p.Hkv * a.nch[b];
+            a.nitems += (p.att_split ? p.Hq : p.Hkv) * a.nch[b];
         }
     }
 }
 
+// Item -> row b, kv head kvh, chunk c, and the item's first q head qh0 (all of
+// the kv head's q heads, or the one q head of an att_split item).
 __device__ __forceinline__ void att_item(const DecodeParams &p, const AttRows &a, int item, int &b, int &kvh,
-                                         int &c) {
+                                         int &c, int &qh0) {
+    const int units = p.att_split ? p.Hq : p.Hkv;
     int base = 0;
     b = 0;
     for (; b < p.B - 1; ++b) {
-        const int cnt = p.Hkv * a.nch[b];
+        const int cnt = units * a.nch[b];
         if (item < base + cnt) break;
         base += cnt;
     }
     const int r = item - base;
-    kvh = r / a.nch[b];
-    c = r - kvh * a.nch[b];
+    const int u = r / a.nch[b];
+    c = r - u * a.nch[b];
+    const int Gq = p.Hq / p.Hkv;
+    kvh = p.att_split ? u / Gq : u;
+    qh0 = p.att_split ? u : u * Gq;
 }
 
 __device__ __forceinline__ float *att_part(const DecodeParams &p, int b, int kvh, int c) {
@@ -637,8 +646,9 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
     const int slot = cta_slot(ph);
     uint32_t done = 0;
     for (int item = slot; item < a.nitems; item += G) {
-        int b, kvh, c;
-        att_item(p, a, item, b, kvh, c);
+        int b, kvh, c, qh0;
+        att_item(p, a, item, b, kvh, c, qh0);
+        const int hl = qh0 - kvh * (p.Hq / p.Hkv);  // first q head within the kv group
         const int pos = ss.pos[b];
         const int t_begin = a.lo[b] + c * p.att_ch;
         const int t_end = min(t_begin + p.att_ch, pos + 1);
@@ -651,7 +661,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
             auto src = [&](int j) {
                 const int i = tid + j * kConsumerThreads;
                 const int vec = i / hd, d = i - vec * hd;
-                return qkv_b + (vec < Gq ? static_cast<int64_t>(kvh * Gq + vec) * hd + d
+                return qkv_b + (vec < Gq ? static_cast<int64_t>(qh0 + vec) * hd + d
                                          : p.A + static_cast<int64_t>((vec == Gq ? 0 : p.Hkv) + kvh) * hd + d);
             };
             uint64_t w[kPer];
@@ -706,7 +716,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
         consumer_sync(kConsumerThreads);
         if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttRoped));
         // ---- K/V write at pos by the chunk that ends there (layers.mojo:57-61)
-        if (t_end == pos + 1 && ss.active[b] && ok) {
+        if (t_end == pos + 1 && ss.active[b] && ok && hl == 0) {  // one item per kv head writes
             const size_t off = static_cast<size_t>(layer) * p.kv_layer_stride + static_cast<size_t>(b) * p.kv_row_stride +
                                static_cast<size_t>(kvh) * p.kv_head_stride + static_cast<size_t>(pos) * hdp;
             for (int d = tid; d < hd; d += kConsumerThreads) {
@@ -833,7 +843,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
             }
             if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttTiles));
             // ---- partial (m, l, acc) of this chunk; combined in the o_proj prologue
-            float *part = att_part(p, b, kvh, c);
+            float *part = att_part(p, b, kvh, c) + hl * (hd + kPartHead);
             const int part_ld = hd + kPartHead;
 #pragma unroll
             for (int k = 0; k < kOut; ++k) {
@@ -936,7 +946,7 @@ __device__ __noinline__ AttRet att_items(const DecodeParams &p, const Smem &sm, 
         }
         if (tid == 0 && done == 0) trace_mark(trace_slot(p, ph, kTrAttTiles));
         // ---- partial (m, l, acc) of this chunk; combined in the o_proj prologue
-        float *part = att_part(p, b, kvh, c);
+        float *part = att_part(p, b, kvh, c) + hl * (hd + kPartHead);
         const int part_ld = hd + kPartHead;
         if (ntq > 1) {  // fold the position classes
             float *red = rope_s + B * hd;  // [ntq][Gq][hd]
@@ -977,6 +987,7 @@ __device__ __forceinline__ AttRet att_dispatch(const DecodeParams &p, const Smem
                                                const LayerPtrs &lp, int layer, int ph, const AttRows &a,
                                                uint32_t tile, bool ok, int tid, bool has_dep) {
     const int Gq = p.Hq / p.Hkv;
+    if (p.att_split && p.hd == 256) return att_items<256, 1>(p, sm, ss, lp, layer, ph, a, tile, ok, tid, has_dep);
 #define MG_ATT(HD_, GQ_) \
     if (p.hd == HD_ && Gq == GQ_) return att_items<HD_, GQ_>(p, sm, ss, lp, layer, ph, a, tile, ok, tid, has_dep);
     MG_ATT(256, 4)
@@ -1447,8 +1458,8 @@ __device__ void producer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             att_rows<NB>(p, lp.is_global != 0, ss.pos, a);
             const int slot = cta_slot(ph);
             for (int item = slot; item < a.nitems; item += G) {
-                int b, kvh, c;
-                att_item(p, a, item, b, kvh, c);
+                int b, kvh, c, qh0;
+                att_item(p, a, item, b, kvh, c, qh0);
                 const int pos = ss.pos[b];
                 const int t_begin = a.lo[b] + c * p.att_ch;
                 const int t_end = min(t_begin + p.att_ch, pos + 1);

@@ -145,7 +145,8 @@ struct mg_model {
     uint64_t *trace = nullptr;  // decode timeline (mg_trace_enable)
     bool trace_on = false;
     uint64_t wait_ns = 0;       // decode-kernel wait budget (0: the default 2 s); mg_set_debug
-    int stall_phase = -1;       // test hook: phase whose outputs CTA 0 withholds; mg_set_debug
+    int stall_phase = -1;       // test hook: phase whose outputs one CTA withholds; mg_set_debug
+    bool no_att_split = false;  // MOGEMMA_B200_ATT_SPLIT=0: attention items per kv head group always
     int max_inflight = 2;       // outstanding bulk copies per CTA (MOGEMMA_B200_INFLIGHT)
     int pf_tiles = 0;           // L2 prefetch distance in tiles (MOGEMMA_B200_PREFETCH)
 
@@ -549,6 +550,7 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     m->G = m->num_sms;  // one persistent CTA per SM
     if (const char *e = getenv("MOGEMMA_B200_INFLIGHT")) m->max_inflight = std::max(1, atoi(e));
     if (const char *e = getenv("MOGEMMA_B200_PREFETCH")) m->pf_tiles = std::max(0, atoi(e));
+    if (const char *e = getenv("MOGEMMA_B200_ATT_SPLIT")) m->no_att_split = atoi(e) == 0;
     m->max_ch = kMaxChunks;
 
     // ---- weights
@@ -893,8 +895,8 @@ static DecodeParams base_params(mg_model *m, int B) {
 
 // Positions per split-KV chunk: up to kMaxChunks chunks per (row, kv head) spread over the CTAs, never more
 // than kMaxChunks for the longest row of the launch, whole tiles.
-static int att_chunk(const mg_model *m, int B, int max_ctx) {
-    const int target = std::max(1, std::min(kMaxChunks, m->G / std::max(1, B * m->Hkv)));
+static int att_chunk(const mg_model *m, int B, int max_ctx, int units) {
+    const int target = std::max(1, std::min(kMaxChunks, m->G / std::max(1, B * units)));
     int ch = std::max((max_ctx + target - 1) / target, (max_ctx + kMaxChunks - 1) / kMaxChunks);
     ch = (ch + kAttTile - 1) / kAttTile * kAttTile;
     return std::max(ch, kAttTile);
@@ -903,7 +905,9 @@ static int att_chunk(const mg_model *m, int B, int max_ctx) {
 static mg_status run_decode(mg_model *m, DecodeParams &p, int max_ctx) {
     if (m->tp > 1 && !m->tp_connected)
         return fail(MG_ERR_INVALID, "tensor-parallel model used before mg_tp_connect");
-    p.att_ch = att_chunk(m, p.B, max_ctx);
+    // batch 1 with head dim 256: an attention item per q head (the CTAs are idle otherwise)
+    p.att_split = (m->hd == 256 && m->Hq > m->Hkv && p.B == 1 && !m->no_att_split) ? 1 : 0;
+    p.att_ch = att_chunk(m, p.B, max_ctx, p.att_split ? m->Hq : m->Hkv);
     // every forward writes its activations with new tags; before the count
     // wraps, the words are cleared so that no old tag can match again
     if (++m->epoch > kMaxEpoch) {
