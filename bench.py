@@ -94,11 +94,12 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def algorithmic_bytes(info, pos0: int, n: int, rows: int = 1) -> float:
+def algorithmic_bytes(info, pos0: int, n: int, rows: int = 1, bf16_copies: bool = False) -> float:
     """Average bytes one decode step (of one rank) must move for positions pos0..pos0+n-1 of `rows` rows.
 
-    Beyond 8 rows the step runs on the batched path, which streams bf16 copies of the weights and writes and
-    reads back [rows, vocab] logits."""
+    The weights count once per step whatever the number of row groups.  On the batched tensor-core path
+    (`bf16_copies`) the step streams bf16 copies of the weights and writes and reads back [rows, vocab]
+    logits."""
     tp = max(1, int(info.tp_size))
     kv_heads = info.num_kv_heads // tp if info.num_kv_heads % tp == 0 else 1  # this rank's kv heads
     kv_row = 2 * kv_heads * info.head_dim * 4  # K+V fp32, one layer, one position
@@ -108,7 +109,7 @@ def algorithmic_bytes(info, pos0: int, n: int, rows: int = 1) -> float:
     logits = info.vocab_size // tp * 4
     emb_row = info.hidden_size * (4 if info.weight_dtype == 0 else 2)
     weights = float(info.weight_bytes_per_step)
-    if rows > 8:
+    if bf16_copies:
         weights = weights / (4 if info.weight_dtype == 0 else 2) * 2
         logits *= 2
     return weights + rows * (kv_read + kv_write + logits + emb_row)
@@ -425,7 +426,8 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled before the timed decode")
     ap.add_argument("--decode", type=int, default=DECODE, help="tokens decoded per step")
     ap.add_argument("--batch", type=int, default=1,
-                    help="decode rows (beyond the persistent kernel's rows: batched tensor-core steps)")
+                    help="decode rows (beyond the persistent kernel's 8 rows: one launch per group of 8 rows, "
+                         "or the batched tensor-core steps with --batched-tc)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "embed"],
                     help="prefill: the batched tensor-core prefill of --prompt tokens; embed: the bidirectional "
                          "encoder on 256 sequences")
@@ -438,6 +440,8 @@ def main() -> None:
     ap.add_argument("--mode", default="ref", choices=["ref", "gemma3"],
                     help="gemma3: sliding window on 5 of 6 layers and dual RoPE theta (the 4B/27B configurations)")
     ap.add_argument("--e2e-passes", type=int, default=10, help="decode passes timed end to end (at least)")
+    ap.add_argument("--batched-tc", action="store_true",
+                    help="prompt and more than 8 rows on the tensor-core path (bf16 weight copies)")
     args = ap.parse_args()
     CONFIG, PROMPT, DECODE = args.model, args.prompt, args.decode
     world, rank, local = dist_setup()
@@ -460,8 +464,10 @@ def main() -> None:
     d = synth.CONFIGS[CONFIG]
     tp = args.parallel == "tp" and world > 1
     B = args.batch
+    # more rows than the persistent kernel holds: one launch per row group in fp32 (prefill_path 0), or with
+    # --batched-tc the tensor-core path on bf16 weight copies (prefill_path 1)
     opts = dict(device=local, capacity=PROMPT + DECODE, max_batch=B, weight_dtype=args.weight_dtype,
-                prefill_path=1 if B > 1 and not tp else 0)
+                prefill_path=1 if args.batched_tc and not tp else 0)
     if args.device_weights:
         # seeded N(0, 0.02) weights generated on each device (models larger than host memory);
         # every rank generates the same full tensors and keeps its shard
@@ -516,7 +522,9 @@ def main() -> None:
     tokens = args.steps * DECODE * streams * B
     value = tokens / (ms / 1000.0)
     ms_launch = ms / (args.steps * DECODE)
-    bytes_launch = algorithmic_bytes(info, PROMPT - 1, DECODE, B)
+    tc_path = B > 8 and args.batched_tc and not tp
+    groups = -(-B // 8)  # decode-kernel launches per token: one per group of up to 8 rows
+    bytes_launch = algorithmic_bytes(info, PROMPT - 1, DECODE, B, bf16_copies=tc_path)
     achieved = bytes_launch / (ms_launch / 1000.0) / 1e9
     pk = peaks()
 
@@ -552,7 +560,7 @@ def main() -> None:
             "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             # more rows than the persistent kernel holds run the batched tensor-core path on bf16 weight copies
-            "dtype": args.weight_dtype if B <= 8 else "bf16 (tcgen05 on bf16 weight copies, fp32 accumulate)",
+            "dtype": args.weight_dtype if not tc_path else "bf16 (tcgen05 on bf16 weight copies, fp32 accumulate)",
             "data": "synthetic (seeded N(0,0.02) random-init weights, uniform random prompt ids)",
             "config": bench_config(world, B, tp, args.weight_dtype),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * DECODE,
@@ -560,14 +568,16 @@ def main() -> None:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"],
                          "traffic": (bytes_launch * TRAFFIC_RATIO[(CONFIG, args.weight_dtype)]
-                                     if (CONFIG, args.weight_dtype) in TRAFFIC_RATIO else None),
+                                     if (CONFIG, args.weight_dtype) in TRAFFIC_RATIO and B <= 8 else None),
                          "traffic_source": "ncu dram__bytes_read+write of a Gemma3-270M launch, scaled by bytes",
-                         "peak_source": pk["source"], "kernel": ("decode_kernel (one launch per token)" if B <= 8 else
-                                    "batched step: tcgen05 GEMMs + prefill kernels per layer, lm_head GEMM, sampler"),
+                         "peak_source": pk["source"],
+                         "kernel": ("batched step: tcgen05 GEMMs + prefill kernels per layer, lm_head GEMM, sampler"
+                                    if tc_path else "decode_kernel (one launch per token)" if B <= 8 else
+                                    f"decode_kernel (one launch per token per group of 8 rows: {groups})"),
                          "algorithmic_bytes_per_launch": bytes_launch},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
-            "gpu_launches": args.steps * DECODE * (1 if B <= 8 else 9 * d.layers + 4),
+            "gpu_launches": args.steps * DECODE * (9 * d.layers + 4 if tc_path else groups),
             "ms_per_token": ms_launch,
         }
         print(json.dumps(line), flush=True)

@@ -125,7 +125,7 @@ struct DecodeParams {
     int32_t V_full;          // vocabulary of the whole model (token id range)
     int32_t vocab_off;       // first vocabulary row of this rank's lm_head shard
     int32_t xB;              // rows per source block in the exchange buffers (the model's max batch)
-    int32_t pad3_;
+    int32_t row_base;        // model row of this launch's row 0 (launches over row groups; Philox row index)
     uint64_t xep;            // exchanges of earlier forwards: layer l exchanges index xep + l
     uint64_t lm_ep;          // candidate exchanges of earlier forwards
     char *xpeer[kMaxTp];     // exchange buffer of every rank (this rank's own at tp_rank)

@@ -196,7 +196,7 @@ struct SmallSmem {
     int pos[kMaxRows];
     int tok[kMaxRows];
     int active[kMaxRows];
-    float red[kConsumerWarps * kMaxRows];
+    float red[kConsumerWarps * kMaxRows * 4];
     uint32_t flag;
     uint32_t pad_;
     uint64_t *tr_ready;  // trace slots of the current phase (consumer thread 0 only)
@@ -229,6 +229,30 @@ __device__ __forceinline__ void block_sum_rows(float (&v)[NB], SmallSmem &ss, in
         for (int w = 0; w < kConsumerWarps; ++w) t += ss.red[w * kMaxRows + b];
         v[b] = t;
     }
+    consumer_sync(kConsumerThreads);
+}
+
+// Sum over the consumer threads of four per-thread values for each of NB rows.
+template <int NB>
+__device__ __forceinline__ void block_sum4_rows(float (&v)[4][NB], SmallSmem &ss, int tid) {
+    const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float s = warp_sum(v[k][b]);
+            if (lane == 0) ss.red[(warp * 4 + k) * kMaxRows + b] = s;
+        }
+    consumer_sync(kConsumerThreads);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) t += ss.red[(w * 4 + k) * kMaxRows + b];
+            v[k][b] = t;
+        }
     consumer_sync(kConsumerThreads);
 }
 
@@ -266,22 +290,38 @@ __device__ __forceinline__ bool stage_norm(const uint64_t *base, const uint64_t 
                                            SmallSmem &ss, int tid, uint32_t *err, uint32_t site, int nadd = 1,
                                            int64_t add_stride = 0) {
     bool ok = true;
-    float sq[NB], sq2[NB];
+    // One block reduction: with a = add * (1 + w_add) and s the add row's RMS
+    // scale, sum(x^2) = sum(base^2) + 2 s sum(base a) + s^2 sum(a^2), so the
+    // four sums sum(add^2), sum(base^2), sum(base a), sum(a^2) give both scales.
+    float sums[4][NB];
 #pragma unroll
-    for (int b = 0; b < NB; ++b) sq[b] = sq2[b] = 0.f;
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) sums[k][b] = 0.f;
     float *xb = xs + NB * Kp;  // base rows staged next to the activation stage
     for (int j0 = 0; j0 * kConsumerThreads < H; j0 += kNormPer) {
+        float wa[kNormPer];
+        if (j0 == 0) {
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) wa[j] = nw.wa[j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < kNormPer; ++j) {
+                const int i = tid + (j0 + j) * kConsumerThreads;
+                wa[j] = i < H ? __ldg(w_add + i) : 0.f;
+            }
+        }
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
             const uint64_t *brow = base + static_cast<int64_t>(b) * H;
             const uint64_t *arow = add_t + static_cast<int64_t>(b) * H;
-            uint64_t wb[kNormPer], wa[kNormPer];
+            uint64_t wb[kNormPer], wv[kNormPer];
             float v[kNormPer];
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
                 const int i = tid + (j0 + j) * kConsumerThreads;
                 wb[j] = i < H ? tg_load(brow + i) : tg_pack(0.f, tag);
-                if constexpr (!XSUM) wa[j] = i < H ? tg_load(arow + i) : tg_pack(0.f, tag);
+                if constexpr (!XSUM) wv[j] = i < H ? tg_load(arow + i) : tg_pack(0.f, tag);
             }
             if constexpr (XSUM) {
                 float t[kMaxTp][kNormPer];
@@ -306,71 +346,63 @@ __device__ __forceinline__ bool stage_norm(const uint64_t *base, const uint64_t 
             ok = tg_settle(wb, tag, bsrc, err, site, g_wait_ns) && ok;
             if constexpr (!XSUM) {
                 auto asrc = [&](int j) { return arow + tid + (j0 + j) * kConsumerThreads; };
-                ok = tg_settle(wa, tag, asrc, err, site, g_wait_ns) && ok;
+                ok = tg_settle(wv, tag, asrc, err, site, g_wait_ns) && ok;
 #pragma unroll
-                for (int j = 0; j < kNormPer; ++j) v[j] = tg_val(wa[j]);
+                for (int j = 0; j < kNormPer; ++j) v[j] = tg_val(wv[j]);
             }
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
                 const int i = tid + (j0 + j) * kConsumerThreads;
+                const float bv = tg_val(wb[j]);
                 if (i < H) {
                     xs[b * Kp + i] = v[j];
-                    xb[b * H + i] = tg_val(wb[j]);
+                    xb[b * H + i] = bv;
                 }
-                sq[b] += v[j] * v[j];
+                const float av = v[j] * (1.0f + wa[j]);
+                sums[0][b] += v[j] * v[j];
+                sums[1][b] += bv * bv;
+                sums[2][b] += bv * av;
+                sums[3][b] += av * av;
             }
         }
     }
-    block_sum_rows<NB>(sq, ss, tid);
-    // The first chunk uses the prefetched weights; later chunks (H > 2048) load
-    // theirs.  Separate branches keep the first chunk free of global loads.
-    for (int j0 = 0; j0 * kConsumerThreads < H; j0 += kNormPer) {
-        float wa[kNormPer];
+    block_sum4_rows<NB>(sums, ss, tid);
+    float inv_a[NB], inv_x[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        inv_a[b] = rms_inv(sums[0][b], inv_h);
+        const float sx = sums[1][b] + 2.0f * inv_a[b] * sums[2][b] + inv_a[b] * inv_a[b] * sums[3][b];
+        inv_x[b] = rms_inv(fmaxf(sx, 0.f), inv_h);
+    }
+    // x = base + add * inv_a * (1 + w_add) -> out; xs = x * inv_x * (1 + w_next), zero padded to Kp
+    for (int j0 = 0; j0 * kConsumerThreads < Kp; j0 += kNormPer) {
+        float wa[kNormPer], wn[kNormPer];
         if (j0 == 0) {
 #pragma unroll
-            for (int j = 0; j < kNormPer; ++j) wa[j] = nw.wa[j];
+            for (int j = 0; j < kNormPer; ++j) {
+                wa[j] = nw.wa[j];
+                wn[j] = nw.wn[j];
+            }
         } else {
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
                 const int i = tid + (j0 + j) * kConsumerThreads;
                 wa[j] = i < H ? __ldg(w_add + i) : 0.f;
-            }
-        }
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-            const float inv = rms_inv(sq[b], inv_h);
-#pragma unroll
-            for (int j = 0; j < kNormPer; ++j) {
-                const int i = tid + (j0 + j) * kConsumerThreads;
-                if (i < H) {
-                    const float x = xb[b * H + i] + xs[b * Kp + i] * inv * (1.0f + wa[j]);
-                    xs[b * Kp + i] = x;
-                    if (out) tg_store(out + static_cast<int64_t>(b) * H + i, x, out_tag);
-                    sq2[b] += x * x;
-                }
-            }
-        }
-    }
-    block_sum_rows<NB>(sq2, ss, tid);
-    for (int j0 = 0; j0 * kConsumerThreads < Kp; j0 += kNormPer) {
-        float wn[kNormPer];
-        if (j0 == 0) {
-#pragma unroll
-            for (int j = 0; j < kNormPer; ++j) wn[j] = nw.wn[j];
-        } else {
-#pragma unroll
-            for (int j = 0; j < kNormPer; ++j) {
-                const int i = tid + (j0 + j) * kConsumerThreads;
                 wn[j] = i < H ? __ldg(w_next + i) : 0.f;
             }
         }
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-            const float inv = rms_inv(sq2[b], inv_h);
 #pragma unroll
             for (int j = 0; j < kNormPer; ++j) {
                 const int i = tid + (j0 + j) * kConsumerThreads;
-                if (i < Kp) xs[b * Kp + i] = i < H ? xs[b * Kp + i] * inv * (1.0f + wn[j]) : 0.0f;
+                if (i < H) {
+                    const float x = xb[b * H + i] + xs[b * Kp + i] * inv_a[b] * (1.0f + wa[j]);
+                    if (out) tg_store(out + static_cast<int64_t>(b) * H + i, x, out_tag);
+                    xs[b * Kp + i] = x * inv_x[b] * (1.0f + wn[j]);
+                } else if (i < Kp) {
+                    xs[b * Kp + i] = 0.0f;
+                }
             }
         }
     }
@@ -1243,7 +1275,7 @@ static __device__ __noinline__ int32_t row_draw(const DecodeParams &p, const Sme
             block_select_topk(n, K, [&](int i) { return keys[i]; }, outk, sel, tid, kConsumerThreads, sync);
         }
     }
-    const double u = p.uniforms ? p.uniforms[b] : philox_uniform(p.seed, p.rng_offset, b);
+    const double u = p.uniforms ? p.uniforms[b] : philox_uniform(p.seed, p.rng_offset, b + p.row_base);
     const int32_t token = draw_block(outk, K, p.temperature, p.top_p, u, fscr, escr, oscr, ish, tid, kConsumerThreads,
                                      sync);
     return (tid == 0 && ok) ? token : -1;

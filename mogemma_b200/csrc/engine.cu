@@ -149,6 +149,7 @@ struct mg_model {
     bool no_att_split = false;  // MOGEMMA_B200_ATT_SPLIT=0: attention items per kv head group always
     int max_inflight = 2;       // outstanding bulk copies per CTA (MOGEMMA_B200_INFLIGHT)
     int pf_tiles = 0;           // L2 prefetch distance in tiles (MOGEMMA_B200_PREFETCH)
+    int att_chunks = kMaxChunks;  // most split-KV chunks per (row, attention unit) (MOGEMMA_B200_ATT_CHUNKS)
 
     // tensor parallelism: Hq, Hkv, A, I, V above are this rank's shard; *_g the model's
     int tp = 1, tp_rank = 0;
@@ -534,10 +535,10 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     if (m->S < 2)
         return fail(MG_ERR_UNSUPPORTED, "activation stage of %d floats leaves no room for the weight ring",
                     m->xs_floats);
-    if (m->Bmax > m->Bdec && (m->prefill_path != 1 || m->tp > 1))
+    if (m->Bmax > m->Bdec && m->tp > 1)
         return fail(MG_ERR_UNSUPPORTED,
-                    "max_batch %d: the persistent decode kernel holds %d rows of this model; more rows need "
-                    "prefill_path 1 (batched tensor-core steps) without tensor parallelism",
+                    "max_batch %d: the persistent decode kernel holds %d rows of this model, and tensor-parallel "
+                    "models run one launch of rows",
                     m->Bmax, m->Bdec);
     m->smem = decode_smem_bytes(m->S, m->xs_floats, L);
     if (m->wdtype == MG_F32) {
@@ -551,6 +552,7 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     if (const char *e = getenv("MOGEMMA_B200_INFLIGHT")) m->max_inflight = std::max(1, atoi(e));
     if (const char *e = getenv("MOGEMMA_B200_PREFETCH")) m->pf_tiles = std::max(0, atoi(e));
     if (const char *e = getenv("MOGEMMA_B200_ATT_SPLIT")) m->no_att_split = atoi(e) == 0;
+    if (const char *e = getenv("MOGEMMA_B200_ATT_CHUNKS")) m->att_chunks = std::min(kMaxChunks, std::max(1, atoi(e)));
     m->max_ch = kMaxChunks;
 
     // ---- weights
@@ -667,7 +669,7 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         CU(cudaMemcpyAsync(m->row_ident, ident.data(), sizeof(int32_t) * m->nrows, cudaMemcpyHostToDevice, m->stream));
         CU(cudaStreamSynchronize(m->stream));
     }
-    if (m->Bmax > m->Bdec) {  // lm_head for batched decode steps
+    if (m->Bmax > m->Bdec && m->prefill_path == 1) {  // lm_head for batched tensor-core decode steps
         TRY(dalloc(m, &m->pf_lm, static_cast<size_t>(m->V) * m->Hp));
         TRY(upload_matrix(m, *lmh, m->V, m->H, m->pf_lm, MG_BF16, m->Hp, staging, staging_bytes));
     }
@@ -896,7 +898,7 @@ static DecodeParams base_params(mg_model *m, int B) {
 // Positions per split-KV chunk: up to kMaxChunks chunks per (row, kv head) spread over the CTAs, never more
 // than kMaxChunks for the longest row of the launch, whole tiles.
 static int att_chunk(const mg_model *m, int B, int max_ctx, int units) {
-    const int target = std::max(1, std::min(kMaxChunks, m->G / std::max(1, B * units)));
+    const int target = std::max(1, std::min(m->att_chunks, m->G / std::max(1, B * units)));
     int ch = std::max((max_ctx + target - 1) / target, (max_ctx + kMaxChunks - 1) / kMaxChunks);
     ch = (ch + kAttTile - 1) / kAttTile * kAttTile;
     return std::max(ch, kAttTile);
@@ -993,6 +995,41 @@ static mg_status validate_rows(mg_model *m, int batch) {
     return MG_OK;
 }
 
+// Rows [r0, r0 + nb) of the model as one launch of nb rows: the row-indexed
+// state (tokens, positions, KV rows, logits rows, drawn tokens, variates, ids)
+// is offset; activations and candidate keys are per-launch scratch.  Steps of
+// more rows than the persistent kernel holds run one launch per row group, in
+// the reference's fp32 arithmetic (models created with prefill_path 0).
+static void row_window(const mg_model *m, DecodeParams &p, int r0, int nb) {
+    p.B = nb;
+    p.row_base = r0;
+    p.tok += r0;
+    p.pos += r0;
+    p.kc += static_cast<int64_t>(r0) * m->kv_row_stride;
+    p.vc += static_cast<int64_t>(r0) * m->kv_row_stride;
+    if (p.logits) p.logits += static_cast<int64_t>(r0) * m->V;
+    if (p.out_tokens) p.out_tokens += r0;
+    if (p.uniforms) p.uniforms += r0;
+    if (p.ids) p.ids += static_cast<int64_t>(r0) * p.ids_ld;
+    if (p.nvalid) p.nvalid += r0;
+    if (p.emb_acc) p.emb_acc += static_cast<int64_t>(r0) * m->H;
+}
+
+// The decode launches of one step for rows [0, batch): one launch when the
+// persistent kernel holds them all, else one per row group.  `p` is a template
+// for rows [0, batch) (lm_mode, sampling, out_tokens, uniforms, ids set).
+static mg_status run_rows(mg_model *m, const DecodeParams &p, int batch, const std::vector<int> &ctx) {
+    for (int r0 = 0; r0 < batch; r0 += m->Bdec) {
+        const int nb = std::min(m->Bdec, batch - r0);
+        DecodeParams q = p;
+        if (batch > m->Bdec) row_window(m, q, r0, nb);
+        int max_ctx = 0;
+        for (int b = r0; b < r0 + nb; ++b) max_ctx = std::max(max_ctx, ctx[b]);
+        TRY(run_decode(m, q, max_ctx));
+    }
+    return MG_OK;
+}
+
 static mg_status step_impl(mg_model *m, int batch, float *logits_host, int32_t *sampled_host, const mg_sampling *s,
                            bool check) {
     for (int b = 0; b < batch; ++b)
@@ -1015,9 +1052,9 @@ static mg_status step_impl(mg_model *m, int batch, float *logits_host, int32_t *
     }
     p.rng_offset = m->rng_offset;
     p.out_tokens = nullptr;
-    int max_ctx = 0;
-    for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, m->h_pos[b] + 1);
-    TRY(run_decode(m, p, max_ctx));
+    std::vector<int> ctx(batch);
+    for (int b = 0; b < batch; ++b) ctx[b] = m->h_pos[b] + 1;
+    TRY(run_rows(m, p, batch, ctx));
     float *logits = m->logits;
     if (m->tp > 1 && (sc.general || logits_host)) {
         TRY(gather_logits(m, batch));
@@ -1059,7 +1096,7 @@ extern "C" mg_status mg_step(mg_model *m, const int32_t *token_ids_host, int32_t
             return fail(MG_ERR_INVALID, "token id %d out of range [0, %d)", token_ids_host[b], m->V_g);
     memcpy(m->pinned, token_ids_host, sizeof(int32_t) * batch);
     CU(cudaMemcpyAsync(m->tok, m->pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, m->stream));
-    if (batch <= m->Bdec) return step_impl(m, batch, logits_host, sampled_host, s, true);
+    if (batch <= m->Bdec || m->prefill_path != 1) return step_impl(m, batch, logits_host, sampled_host, s, true);
     // more rows than the persistent kernel holds: batched tensor-core step
     for (int b = 0; b < batch; ++b)
         if (m->h_pos[b] >= m->cap) return fail(MG_ERR_SEQ_EXCEEDED, "Sequence length exceeded");
@@ -1108,9 +1145,10 @@ extern "C" mg_status mg_generate(mg_model *m, int32_t n_steps, int32_t batch, co
     }
     const SampleCfg sc = sample_cfg(m, s);
     const std::vector<int32_t> pos0 = m->h_pos;
-    for (int t = 0; t < n_steps && batch > m->Bdec; ++t)  // batched tensor-core steps
+    const bool tc_steps = batch > m->Bdec && m->prefill_path == 1;
+    for (int t = 0; t < n_steps && tc_steps; ++t)  // batched tensor-core steps
         TRY(step_batched(m, batch, nullptr, s, m->out_tokens + static_cast<int64_t>(t) * batch));
-    for (int t = 0; t < n_steps && batch <= m->Bdec; ++t) {
+    for (int t = 0; t < n_steps && !tc_steps; ++t) {  // decode-kernel launches (per row group)
         DecodeParams p = base_params(m, batch);
         p.lm_mode = kLmLogits;
         p.topk = sc.fused ? sc.topk : 0;
@@ -1120,9 +1158,9 @@ extern "C" mg_status mg_generate(mg_model *m, int32_t n_steps, int32_t batch, co
         p.top_k_req = s->top_k;
         p.rng_offset = m->rng_offset;
         p.out_tokens = m->out_tokens + static_cast<int64_t>(t) * batch;
-        int max_ctx = 0;
-        for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, m->h_pos[b] + 1);
-        TRY(run_decode(m, p, max_ctx));
+        std::vector<int> ctx(batch);
+        for (int b = 0; b < batch; ++b) ctx[b] = m->h_pos[b] + 1;
+        TRY(run_rows(m, p, batch, ctx));
         if (sc.general) {
             float *logits = m->logits;
             if (m->tp > 1) {
@@ -1366,9 +1404,6 @@ extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, cons
         }
         return st;
     }
-    if (batch > m->Bdec)
-        return fail(MG_ERR_UNSUPPORTED, "prefill of %d rows needs prefill_path 1 (the decode kernel holds %d)", batch,
-                    m->Bdec);
     for (int t = 0; t < longest; ++t) {
         DecodeParams p = base_params(m, batch);
         p.lm_mode = kLmNone;
@@ -1376,9 +1411,9 @@ extern "C" mg_status mg_prefill(mg_model *m, const int32_t *token_ids_host, cons
         p.ids_ld = max_len;
         p.nvalid = m->nvalid;
         p.step_t = t;
-        int max_ctx = 0;
-        for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, pos0[b] + std::min(t, lens_host[b]) + 1);
-        TRY(run_decode(m, p, max_ctx));
+        std::vector<int> ctx(batch);
+        for (int b = 0; b < batch; ++b) ctx[b] = pos0[b] + std::min(t, lens_host[b]) + 1;
+        TRY(run_rows(m, p, batch, ctx));
     }
     // the last fed token becomes the current token of each row
     for (int b = 0; b < batch; ++b) m->h_pos[b] = pos0[b] + lens_host[b];

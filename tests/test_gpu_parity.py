@@ -136,6 +136,26 @@ def test_batched_rows_match_independent_runs() -> None:
         close_logits(lg[i], ref.step(r[-1]))
 
 
+def test_rows_beyond_the_kernel_rows_in_fp32() -> None:
+    """12 rows on a model created with prefill_path 0: the decode kernel runs one launch per row group
+    (8 + 4 rows), each row in the reference's fp32 arithmetic at its own position."""
+    w, llm = build(TINY, max_batch=12, capacity=64)
+    rows = [[int(t) for t in synth.prompt_ids(3 + 2 * i, TINY.vocab, seed=50 + i)] for i in range(12)]
+    _core.prefill_rows(llm, [r[:-1] for r in rows])
+    assert llm["_handle"].get_pos()[:12] == [len(r) - 1 for r in rows]
+    lg, drawn = _core.step_rows(llm, [r[-1] for r in rows], sampling=(0.0, 0, 1.0))
+    for i, r in enumerate(rows):
+        ref = oracle.RefModel(w, max_seq_len=64)
+        for t in r[:-1]:
+            ref.step_no_logits(t)
+        close_logits(lg[i], ref.step(r[-1]))
+        assert int(drawn[i]) == int(np.argmax(lg[i]))
+    # sampled draws of the second group use their own Philox rows: a fixed seed repeats them
+    us = np.linspace(0.05, 0.95, 12)
+    _, tok = _core.step_rows(llm, [int(t) for t in drawn], sampling=(0.8, 20, 1.0), uniforms=us)
+    assert ((tok >= 0) & (tok < TINY.vocab)).all()
+
+
 @pytest.mark.parametrize("params", [(0.0, 50, 1.0), (0.7, 64, 1.0), (0.7, 10, 0.9), (1.0, 3, 1.0)])
 def test_fused_draw_matches_rules_on_device_logits(params: tuple[float, int, float]) -> None:
     w, llm = build(TINY)
