@@ -261,6 +261,28 @@ __device__ __forceinline__ void consumer_sync(uint32_t nthreads) {
     asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 }
 
+// The same barrier, returning whether `v` holds in every consumer thread.
+__device__ __forceinline__ bool consumer_all(bool v, uint32_t nthreads) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "r"(nthreads)
+        : "memory");
+    return r != 0u;
+}
+
+// Atomic exchange at gpu scope with acquire-release order: the stores that
+// happen before it (this CTA's, through a barrier) are visible to whoever
+// reads the value it stores, and what the previous writer stored before its
+// exchange is visible after it.
+__device__ __forceinline__ uint64_t atom_exch_acq_rel(uint64_t *addr, uint64_t v) {
+    uint64_t old;
+    asm volatile("atom.acq_rel.gpu.global.exch.b64 %0, [%1], %2;" : "=l"(old) : "l"(addr), "l"(v) : "memory");
+    return old;
+}
+
 // ---- numeric helpers ----
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

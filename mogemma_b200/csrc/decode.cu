@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include "decode.cuh"
 
@@ -37,7 +39,7 @@ size_t decode_static_smem() {
 }
 
 template <typename WT>
-cudaError_t decode_prepare(size_t dynamic_smem) {
+static cudaError_t decode_prepare_all(size_t dynamic_smem) {
     cudaError_t e = cudaSuccess;
     if ((e = decode_prepare_nb<WT, 1>(dynamic_smem)) != cudaSuccess) return e;
     if ((e = decode_prepare_nb<WT, 2>(dynamic_smem)) != cudaSuccess) return e;
@@ -47,6 +49,24 @@ cudaError_t decode_prepare(size_t dynamic_smem) {
     if ((e = decode_prepare_nb<WT, 6>(dynamic_smem)) != cudaSuccess) return e;
     if ((e = decode_prepare_nb<WT, 7>(dynamic_smem)) != cudaSuccess) return e;
     return decode_prepare_nb<WT, 8>(dynamic_smem);
+}
+
+template <typename WT>
+cudaError_t decode_prepare(size_t dynamic_smem) {
+    // The attribute is the kernel's allowance on this device, shared by every
+    // model of the process: it is only ever raised, so that a model created
+    // later with a smaller stage cannot make an earlier model's launches fail.
+    static std::mutex mu;
+    static std::map<int, size_t> allowed;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t &cur = allowed[dev];
+    if (dynamic_smem <= cur) return cudaSuccess;
+    e = decode_prepare_all<WT>(dynamic_smem);
+    if (e == cudaSuccess) cur = dynamic_smem;
+    return e;
 }
 
 // Smallest occupancy over the row counts (every launch shape must fit).

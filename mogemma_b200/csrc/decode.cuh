@@ -26,6 +26,8 @@ constexpr int kMaxQPerKv = 8;
 constexpr int kMaxTopK = 64;         // fused top-k width
 constexpr int kAttTile = 16;         // positions per attention tile
 constexpr int kPartHead = 4;         // floats before a split-KV partial's acc: m, l, 2 pad (16-byte aligned acc)
+constexpr int kSplitVals = 2 * 16 * kMaxRows;  // (gate, up) x rows of a group (<= 16) x kernel rows
+constexpr int kSplitKinds = 5;          // indexed by phase kind (QKV, ATT unused, O, GU, D)
 constexpr int kMaxChunks = 32;       // split-KV chunks per (row, kv head); one warp lane each in the combine
 constexpr int kMaxLayers = 64;       // layers a model may have (tags hold epoch * kMaxLayers + layer)
 constexpr uint32_t kMaxEpoch = (1u << 26) - 1;  // forwards before the tagged buffers are cleared and the count restarts
@@ -107,6 +109,12 @@ struct DecodeParams {
     uint64_t wait_ns;     // budget of every bounded wait (0: the default, kWaitBudgetNs)
     int32_t stall_phase;  // test hook: one CTA withholds its outputs of this phase (-1: none)
     int32_t att_split;    // 1: attention items per q head (head dim 256 only); 0: per kv head group
+    int32_t gemv_split;   // 1: projection phases may split a row group between two CTAs (see gemv_geom)
+    int32_t pad5_;
+    // split row groups: partial row sums [kind][boundary G][part 2][kSplitVals] and one
+    // exchange word per (kind, boundary) -- inside the tagged block, so cleared with it
+    float *split_part;
+    uint64_t *split_tag;
     uint32_t *sync;   // phase counters [n_phases], att_done [L], att_cnt [B*Hkv], exit [1]
     uint32_t *err;    // device error word
     int32_t n_phases;

@@ -63,14 +63,35 @@ __device__ __forceinline__ void phase_of(int ph, int L, int &kind, int &layer) {
 // Rotating slot so the CTAs that get one extra row differ from phase to phase.
 __device__ __forceinline__ int cta_slot(int ph) { return static_cast<int>((blockIdx.x + 61u * ph) % gridDim.x); }
 
+// A CTA's share of a projection phase, as a schedule of row groups:
+//   whole groups [full_g0, full_g0 + nfull) (= row0, nrows, ngroups, tiles),
+//   all segments; then, with a split, the tail of group lead_g (segments
+//   [lead_s0, nseg)), whose head the previous slot computes, and the head of
+//   group tail_g (segments [0, tail_s1)), whose tail the next slot computes.
+// The two CTAs of a split group exchange partial row sums; the second to
+// arrive adds them and writes the rows (gemv_split_rows).
 template <typename WT>
 struct GemvGeom {
     const WT *tiles;  // this CTA's first tile (tiled layout, see tile_shape)
+    const WT *base;   // tile (group 0, segment 0) of the matrix
     bool pair;        // gate/up phase: each tile holds gate rows then up rows
-    int64_t row0;     // first output row of this CTA
+    bool split;       // the schedule holds split groups
+    int64_t row0;     // first output row of this CTA (whole-group schedules)
     int nrows;        // output rows of this CTA (the last group may be partial)
+    int N;            // output rows of the matrix
     int Kp, kc, nseg, rps, ngroups;
     int tile_elems;
+    int kind, slot, layer;
+    int full_g0, nfull;
+    int lead_g, lead_s0;  // lead_g < 0: none
+    int tail_g, tail_s1;  // tail_g < 0: none
+    // split piece k (0: the lead group's tail, 1: the tail group's head); false if absent
+    __device__ __forceinline__ bool split_piece(int k, int &grp, int &s0, int &s1) const {
+        grp = k == 0 ? lead_g : tail_g;
+        s0 = k == 0 ? lead_s0 : 0;
+        s1 = k == 0 ? nseg : tail_s1;
+        return grp >= 0;
+    }
 };
 
 template <typename WT>
@@ -122,6 +143,44 @@ __device__ __forceinline__ void gemv_geom(const DecodeParams &p, const LayerPtrs
     g.nrows = static_cast<int>(min(static_cast<int64_t>(N), static_cast<int64_t>(g1) * g.rps) - g.row0);
     if (g.nrows < 0) g.nrows = 0;
     g.tiles = base + static_cast<int64_t>(g0) * g.nseg * g.tile_elems;
+    // The host marks the phase kinds whose whole groups leave some CTAs two or
+    // more tiles above the even share (split_kinds, engine.cu); their (group,
+    // segment) tiles are split evenly instead.  Every slot then holds at least
+    // nseg tiles, so a group is shared by two slots at most.
+    // (bf16 weights only: the fp32 kernels compile without it, exactly as before it existed)
+    g.split = sizeof(WT) == 2 && ((p.gemv_split >> kind) & 1);
+    if constexpr (sizeof(WT) != 2) return;
+    if (g.split) {
+        const int G = static_cast<int>(gridDim.x);
+        const int U = groups * g.nseg;
+        g.N = N;
+        g.base = base;
+        g.kind = kind;
+        g.slot = slot;
+        int k2;
+        phase_of(ph, p.L, k2, g.layer);
+        g.lead_g = g.tail_g = -1;
+        g.lead_s0 = g.tail_s1 = 0;
+        const int u0 = U * slot / G, u1 = U * (slot + 1) / G;
+        const int ga = u0 / g.nseg, sa = u0 - ga * g.nseg;
+        const int gb = u1 / g.nseg, sb = u1 - gb * g.nseg;
+        g.full_g0 = sa ? ga + 1 : ga;
+        g.nfull = gb - g.full_g0;
+        if (sa) {
+            g.lead_g = ga;
+            g.lead_s0 = sa;
+        }
+        if (sb) {
+            g.tail_g = gb;
+            g.tail_s1 = sb;
+        }
+        // the whole-group fields describe the full groups (streamed first)
+        g.ngroups = g.nfull;
+        g.row0 = static_cast<int64_t>(g.full_g0) * g.rps;
+        g.nrows = static_cast<int>(min(static_cast<int64_t>(N), static_cast<int64_t>(gb) * g.rps) - g.row0);
+        if (g.nrows < 0) g.nrows = 0;
+        g.tiles = base + static_cast<int64_t>(g.full_g0) * g.nseg * g.tile_elems;
+    }
 }
 
 // Attention work split: items are (row, unit, chunk of att_ch positions), a
@@ -198,7 +257,7 @@ struct SmallSmem {
     int active[kMaxRows];
     float red[kConsumerWarps * kMaxRows * 4];
     uint32_t flag;
-    uint32_t pad_;
+    uint32_t split_second;  // gemv_split_rows: this CTA completes the split group
     uint64_t *tr_ready;  // trace slots of the current phase (consumer thread 0 only)
     uint64_t *tr_end;
 };
@@ -536,7 +595,48 @@ __device__ __forceinline__ void gemv_store(const GemvOut &o, int64_t idx, float 
 
 // NB (rows of x) and PAIR (gate/up) are compile-time so the inner loop is a
 // straight run of 128-bit shared loads and FMAs with accumulators in
-// registers.
+// registers.  One tile of a split group: segment s, accumulated into acc/acc2.
+template <typename WT, int NB, bool PAIR>
+__device__ __forceinline__ void gemv_tile(const GemvGeom<WT> &g, const float *__restrict__ xs, const Smem &sm, int S,
+                                       uint32_t tile, int s, int nr, uint32_t *err, bool &ok, int lane, int warp,
+                                       float (&acc)[sizeof(WT) == 2 ? 2 : 1][NB],
+                                       float (&acc2)[sizeof(WT) == 2 ? 2 : 1][NB]) {
+    constexpr int rpw = sizeof(WT) == 2 ? 2 : 1;
+    const int Kp = g.Kp;
+    const int st = static_cast<int>(tile % S);
+    const uint32_t par = (tile / S) & 1u;
+    if (ok) ok = mbar_wait(&sm.full[st], par, err, kErrTimeoutFull | 1u, g_wait_ns);
+    const int c0 = s * g.kc;
+    const int sw = min(g.kc, Kp - c0);
+    const WT *stage = reinterpret_cast<const WT *>(sm.ring + static_cast<size_t>(st) * kStageBytes);
+    const float *xseg = xs + c0;
+    if (ok && warp * rpw < nr) {
+        const WT *wr = stage + static_cast<size_t>(warp * rpw) * g.kc;
+#pragma unroll 2
+        for (int c = lane * 4; c < sw; c += 128) {
+            float4 x4[NB];
+#pragma unroll
+            for (int b = 0; b < NB; ++b) x4[b] = *reinterpret_cast<const float4 *>(xseg + b * Kp + c);
+#pragma unroll
+            for (int k = 0; k < rpw; ++k) {
+                const float4 w4 = lds_w4(wr + k * g.kc + c);
+#pragma unroll
+                for (int b = 0; b < NB; ++b)
+                    acc[k][b] += w4.x * x4[b].x + w4.y * x4[b].y + w4.z * x4[b].z + w4.w * x4[b].w;
+                if constexpr (PAIR) {
+                    const float4 u4 = lds_w4(wr + (g.rps + k) * g.kc + c);
+#pragma unroll
+                    for (int b = 0; b < NB; ++b)
+                        acc2[k][b] += u4.x * x4[b].x + u4.y * x4[b].y + u4.z * x4[b].z + u4.w * x4[b].w;
+                }
+            }
+        }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[st]);
+}
+
+// Whole groups [row0, row0 + nrows) of this CTA (the same inner loop as gemv_tile, kept inline here).
 template <typename WT, int NB, bool PAIR>
 __device__ __forceinline__ void gemv_tiles(const GemvGeom<WT> &g, const float *__restrict__ xs, const Smem &sm, int S,
                                         uint32_t &tile, uint32_t *err, bool &ok, int tid, uint64_t *tr_first,
@@ -605,14 +705,103 @@ __device__ __forceinline__ void gemv_tiles(const GemvGeom<WT> &g, const float *_
     }
 }
 
+// Partial row sums of a split group [kind][boundary][part][kSplitVals].
+__device__ __forceinline__ float *split_slot(const DecodeParams &p, int kind, int bnd, int part) {
+    return p.split_part + (static_cast<int64_t>(kind * static_cast<int>(gridDim.x) + bnd) * 2 + part) * kSplitVals;
+}
+
+// Second half of a split group's epilogue.  Each CTA has stored its partial
+// sums (index (row * NB + b) * 2 + {gate, up}) in its part's slot; thread 0
+// then exchanges the (forward, layer) tag into the boundary's word.  The CTA
+// that finds the same tag there arrived second: it adds the two halves and
+// writes the rows.  Nobody waits, so nothing can hang here; a CTA that failed
+// or withholds its outputs (test hook) does not exchange, and the group's rows
+// stay unwritten, as the readers' bounded waits expect.
+template <int NB, bool PAIR>
+static __device__ __noinline__ void gemv_split_rows(const DecodeParams &p, SmallSmem &ss, int kind, int bnd,
+                                                    int layer, int64_t row0, int nr, GemvOut o, bool ok, int tid) {
+    const bool all_ok = consumer_all(ok, kConsumerThreads);
+    if (tid == 0) {
+        uint32_t second = 0u;
+        if (all_ok && !o.mute) {
+            const uint64_t v = (1ull << 63) | tag_of(p, layer);
+            second = atom_exch_acq_rel(p.split_tag + kind * static_cast<int>(gridDim.x) + bnd, v) == v ? 1u : 0u;
+        }
+        ss.split_second = second;
+    }
+    consumer_sync(kConsumerThreads);
+    if (ss.split_second != 0u && tid < nr * NB) {
+        const int j = tid / NB, b = tid - j * NB;
+        const int i = (j * NB + b) * 2;
+        const float *head = split_slot(p, kind, bnd, 0), *tail = split_slot(p, kind, bnd, 1);
+        const float d = __ldcg(head + i) + __ldcg(tail + i);
+        float v = d;
+        if constexpr (PAIR) {
+            const float u = __ldcg(head + i + 1) + __ldcg(tail + i + 1);
+            const float gelu = 0.5f * d * (1.0f + erff(d * kInvSqrt2));
+            v = gelu * u;
+        }
+        gemv_store(o, b * o.ld + row0 + j, v);
+    }
+}
+
+// The split groups of this CTA, after its whole groups: the lead group's tail
+// (part 1), then the tail group's head (part 0).  Out of line, with its
+// arguments by value, so that the whole-group path around the call compiles
+// as it does without it.  Returns the tile counter, and `ok` in bit 32.
+template <typename WT, int NB, bool PAIR>
+static __device__ __noinline__ uint64_t gemv_split_pieces(const DecodeParams &p, SmallSmem &ss, const GemvGeom<WT> g,
+                                                          const float *__restrict__ xs, const Smem &sm, int S,
+                                                          uint32_t tile, uint32_t *err, bool ok, int tid, GemvOut o) {
+    constexpr int rpw = sizeof(WT) == 2 ? 2 : 1;
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int k = 0; k < 2; ++k) {
+        int grp, s0, s1;
+        if (!g.split_piece(k, grp, s0, s1)) continue;
+        const int part = k == 0 ? 1 : 0;
+        const int nr = min(g.rps, g.N - grp * g.rps);
+        float acc[rpw][NB], acc2[rpw][NB];
+#pragma unroll
+        for (int r = 0; r < rpw; ++r)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) acc[r][b] = acc2[r][b] = 0.f;
+        for (int s = s0; s < s1; ++s, ++tile) gemv_tile<WT, NB, PAIR>(g, xs, sm, S, tile, s, nr, err, ok, lane, warp, acc, acc2);
+        const int bnd = part == 0 ? g.slot : g.slot - 1;
+        float *mine = split_slot(p, g.kind, bnd, part);
+#pragma unroll
+        for (int r = 0; r < rpw; ++r) {
+            const int j = warp * rpw + r;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                const float d = warp_sum(acc[r][b]);
+                const float u = PAIR ? warp_sum(acc2[r][b]) : 0.f;
+                if (lane == 0 && j < nr && ok) {
+                    mine[(j * NB + b) * 2] = d;
+                    mine[(j * NB + b) * 2 + 1] = u;
+                }
+            }
+        }
+        gemv_split_rows<NB, PAIR>(p, ss, g.kind, bnd, g.layer, static_cast<int64_t>(grp) * g.rps, nr, o, ok, tid);
+    }
+    return (static_cast<uint64_t>(ok) << 32) | tile;
+}
+
 template <typename WT, int NB>
-__device__ __forceinline__ void gemv_consume(const GemvGeom<WT> &g, const float *xs, const Smem &sm, int S,
-                                             uint32_t &tile, uint32_t *err, bool &ok, int tid, uint64_t *tr_first,
-                                             GemvOut o) {
+__device__ __forceinline__ void gemv_consume(const DecodeParams &p, SmallSmem &ss, const GemvGeom<WT> &g,
+                                             const float *xs, const Smem &sm, int S, uint32_t &tile, uint32_t *err,
+                                             bool &ok, int tid, uint64_t *tr_first, GemvOut o) {
     if (g.pair)
         gemv_tiles<WT, NB, true>(g, xs, sm, S, tile, err, ok, tid, tr_first, o);
     else
         gemv_tiles<WT, NB, false>(g, xs, sm, S, tile, err, ok, tid, tr_first, o);
+    if constexpr (sizeof(WT) == 2) {
+        if (g.split) {
+            const uint64_t r = g.pair ? gemv_split_pieces<WT, NB, true>(p, ss, g, xs, sm, S, tile, err, ok, tid, o)
+                                      : gemv_split_pieces<WT, NB, false>(p, ss, g, xs, sm, S, tile, err, ok, tid, o);
+            tile = static_cast<uint32_t>(r);
+            ok = (r >> 32) != 0;
+        }
+    }
 }
 
 // ---------------------------------------------------------------- attention
@@ -1329,7 +1518,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                 }
             }
             if (tid == 0) trace_mark(ss.tr_ready);
-            gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+            gemv_consume<WT, NB>(p, ss, g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                                  muted(gemv_out_tagged(p.qkv, p.qkv_rows, tag)));
             phase_done(ss, tid);
         } else if (kind == PH_ATT) {
@@ -1350,7 +1539,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                      ok;
             att_combine(p, ss.att, g.Kp, sm.xs, tid);
             // with tensor parallelism the row-split o_proj partials go to every rank
-            gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+            gemv_consume<WT, NB>(p, ss, g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                                  muted(TP ? gemv_out_peers(ss.xdst_o, p.tp, p.H) : gemv_out_tagged(p.o_raw, p.H, tag)));
             phase_done(ss, tid);
             if constexpr (TP) xsignal(p, 0, tid);
@@ -1372,7 +1561,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                                     p.inv_h, g.Kp, sm.xs, ss, tid, p.err, 100 + ph) && ok;
             }
             if (tid == 0) trace_mark(ss.tr_ready);
-            gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+            gemv_consume<WT, NB>(p, ss, g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                                  muted(gemv_out_float(p.act, p.Ip)));
             cta_signal(ctr_phase(p, ph), mute ? 0u : 1u, ss, tid);
         } else if (kind == PH_D) {
@@ -1398,7 +1587,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                 }
             }
             consumer_sync(kConsumerThreads);
-            gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+            gemv_consume<WT, NB>(p, ss, g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                                  muted(TP ? gemv_out_peers(ss.xdst_d, p.tp, p.H) : gemv_out_tagged(p.mlp_raw, p.H, tag)));
             phase_done(ss, tid);
             if constexpr (TP) xsignal(p, 1, tid);
@@ -1427,7 +1616,7 @@ __device__ void consumer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                             for (int i = tid; i < p.H; i += kConsumerThreads)
                                 p.emb_acc[static_cast<int64_t>(b) * p.H + i] += sm.xs[b * g.Kp + i];
             } else if (p.lm_mode == kLmLogits) {
-                gemv_consume<WT, NB>(g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
+                gemv_consume<WT, NB>(p, ss, g, sm.xs, sm, p.S, tile, p.err, ok, tid, trace_slot(p, ph, kTrPrologue),
                                      muted(gemv_out_float(p.logits, p.V)));
                 if (p.topk > 0) {
                     consumer_sync(kConsumerThreads);
@@ -1522,7 +1711,7 @@ __device__ void producer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
             // this CTA's tiles are contiguous in the tiled layout: one bulk copy per tile
             const uint32_t bytes = static_cast<uint32_t>(g.tile_elems * sizeof(WT));
             const int ntiles = g.ngroups * g.nseg;
-            if (p.pf_tiles > 0 && ok && ntiles > static_cast<int>(S)) {
+            if (p.pf_tiles > 0 && ok && !g.split && ntiles > static_cast<int>(S)) {
                 // L2 prefetch of the part of this phase the ring cannot hold yet
                 const char *from = reinterpret_cast<const char *>(g.tiles) + static_cast<size_t>(S) * bytes;
                 size_t left = static_cast<size_t>(ntiles - static_cast<int>(S)) * bytes;
@@ -1541,6 +1730,21 @@ __device__ void producer_run(const DecodeParams &p, const Smem &sm, SmallSmem &s
                 mbar_arrive_expect_tx(&sm.full[st], bytes);
                 bulk_g2s(sm.ring + static_cast<size_t>(st) * kStageBytes, g.tiles + static_cast<int64_t>(t) * g.tile_elems,
                          bytes, &sm.full[st], pol_w);
+            }
+            // then the split groups' parts, in the consumers' order (gemv_split_pieces)
+            for (int k = 0; sizeof(WT) == 2 && g.split && k < 2; ++k) {
+                int grp, s0, s1;
+                if (!g.split_piece(k, grp, s0, s1)) continue;
+                for (int sg = s0; sg < s1; ++sg, ++tile) {
+                    const int st = static_cast<int>(tile % S);
+                    ok = ok && acquire_slot(tile);
+                    if (!ok) continue;
+                    issued = tile + 1;
+                    mbar_arrive_expect_tx(&sm.full[st], bytes);
+                    bulk_g2s(sm.ring + static_cast<size_t>(st) * kStageBytes,
+                             g.base + (static_cast<int64_t>(grp) * g.nseg + sg) * g.tile_elems, bytes, &sm.full[st],
+                             pol_w);
+                }
             }
         }
         trace_mark(trace_slot(p, ph, kTrProdEnd));

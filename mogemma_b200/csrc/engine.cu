@@ -130,6 +130,10 @@ struct mg_model {
     int64_t kv_layer_stride = 0, kv_row_stride = 0, kv_head_stride = 0;
     // decode activations as tagged words (value + tag of the forward and layer that wrote them)
     uint64_t *h = nullptr, *r = nullptr, *qkv = nullptr, *o_raw = nullptr, *mlp_raw = nullptr;
+    uint64_t *split_tag = nullptr;  // exchange words of split row groups [kSplitKinds][G] (tagged block)
+    float *split_part = nullptr;    // their partial row sums [kSplitKinds][G][2][kSplitVals]
+    bool gemv_split = true;         // MOGEMMA_B200_SPLIT=0: whole row groups per CTA only
+    int split_mask = 0;             // phase kinds (bit PH_*) whose row groups are split (split_kinds)
     size_t tagged_words = 0;   // h .. mlp_raw, allocated as one block
     float *act = nullptr, *attn_part = nullptr;
     uint32_t epoch = 0;        // forwards run so far (tags of the next one use epoch + 1)
@@ -195,6 +199,8 @@ struct mg_model {
     // stages (shared memory); steps with more rows take the batched path
     int Bdec = 1, nrows = kMaxRows;
 };
+
+static int split_kinds(const mg_model *m);
 
 template <typename T>
 static mg_status dalloc(mg_model *m, T **p, size_t count, bool zero = true) {
@@ -553,6 +559,8 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     if (const char *e = getenv("MOGEMMA_B200_PREFETCH")) m->pf_tiles = std::max(0, atoi(e));
     if (const char *e = getenv("MOGEMMA_B200_ATT_SPLIT")) m->no_att_split = atoi(e) == 0;
     if (const char *e = getenv("MOGEMMA_B200_ATT_CHUNKS")) m->att_chunks = std::min(kMaxChunks, std::max(1, atoi(e)));
+    if (const char *e = getenv("MOGEMMA_B200_SPLIT")) m->gemv_split = atoi(e) != 0;
+    m->split_mask = split_kinds(m);
     m->max_ch = kMaxChunks;
 
     // ---- weights
@@ -725,22 +733,23 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
     // ---- activations
     const int B = m->Bmax;
     {  // one zeroed block (tag 0 is never expected), each part 256-byte aligned
-        const size_t sizes[5] = {static_cast<size_t>(B) * m->H, static_cast<size_t>(B) * m->H,
+        const size_t sizes[6] = {static_cast<size_t>(B) * m->H, static_cast<size_t>(B) * m->H,
                                  static_cast<size_t>(B) * m->qkv_rows, static_cast<size_t>(B) * m->H,
-                                 static_cast<size_t>(B) * m->H};
+                                 static_cast<size_t>(B) * m->H, static_cast<size_t>(kSplitKinds) * m->G};
         size_t total = 0;
         for (size_t n : sizes) total += (n + 31) / 32 * 32;
         uint64_t *blk = nullptr;
         TRY(dalloc(m, &blk, total));
         m->tagged_words = total;
-        uint64_t **dst[5] = {&m->h, &m->r, &m->qkv, &m->o_raw, &m->mlp_raw};
+        uint64_t **dst[6] = {&m->h, &m->r, &m->qkv, &m->o_raw, &m->mlp_raw, &m->split_tag};
         size_t off = 0;
-        for (int k = 0; k < 5; ++k) {
+        for (int k = 0; k < 6; ++k) {
             *dst[k] = blk + off;
             off += (sizes[k] + 31) / 32 * 32;
         }
     }
     TRY(dalloc(m, &m->act, static_cast<size_t>(B) * m->Ip));
+    TRY(dalloc(m, &m->split_part, static_cast<size_t>(kSplitKinds) * m->G * 2 * kSplitVals));
     TRY(dalloc(m, &m->attn_part, static_cast<size_t>(B) * m->Hkv * m->max_ch * Gq * (hd + kPartHead)));
     if (m->tp > 1) {
         // exchange buffer: counters, o_proj / down_proj partials [tp][Bmax][H],
@@ -864,6 +873,9 @@ static DecodeParams base_params(mg_model *m, int B) {
     p.act = m->act;
     p.mlp_raw = m->mlp_raw;
     p.attn_part = m->attn_part;
+    p.split_part = m->split_part;
+    p.split_tag = m->split_tag;
+    p.gemv_split = m->gemv_split ? m->split_mask : 0;
     p.logits = m->logits;
     p.cand_key = m->cand_key;
     p.emb_acc = m->emb_acc;
@@ -897,6 +909,33 @@ static DecodeParams base_params(mg_model *m, int B) {
 
 // Positions per split-KV chunk: up to kMaxChunks chunks per (row, kv head) spread over the CTAs, never more
 // than kMaxChunks for the longest row of the launch, whole tiles.
+// Projection phases whose whole row groups leave some CTAs two or more tiles
+// above the even share (Gemma3-4B down_proj: 160 groups of 10 tiles on 148
+// CTAs): the kernel splits their (group, segment) tiles evenly instead, two
+// CTAs sharing a group where a slot boundary falls inside it (gemv_geom).
+// Every slot must hold at least nseg tiles, so a group has two owners at most.
+// Only the bf16 kernels carry the split (the large models); the fp32 kernels
+// stay without it.
+static int split_kinds(const mg_model *m) {
+    if (m->wdtype == MG_F32) return 0;
+    const int esz = 2;
+    const struct {
+        int kind, N, Kp;
+        bool pair;
+    } phases[4] = {{PH_QKV, m->qkv_rows, m->Hp, false},
+                   {PH_O, m->H, m->Ap, false},
+                   {PH_GU, m->I, m->Hp, true},
+                   {PH_D, m->H, m->Ip, false}};
+    int mask = 0;
+    for (const auto &f : phases) {
+        const TileShape ts = tile_shape(f.Kp, esz, f.pair);
+        const int64_t G = m->G, groups = (f.N + ts.rps - 1) / ts.rps, U = groups * ts.nseg;
+        if (ts.nseg < 2 || U / G < ts.nseg || U * G >= (int64_t{1} << 31)) continue;
+        if ((groups + G - 1) / G * ts.nseg - (U + G - 1) / G >= 2) mask |= 1 << f.kind;
+    }
+    return mask;
+}
+
 static int att_chunk(const mg_model *m, int B, int max_ctx, int units) {
     const int target = std::max(1, std::min(m->att_chunks, m->G / std::max(1, B * units)));
     int ch = std::max((max_ctx + target - 1) / target, (max_ctx + kMaxChunks - 1) / kMaxChunks);

@@ -156,6 +156,75 @@ def test_rows_beyond_the_kernel_rows_in_fp32() -> None:
     assert ((tok >= 0) & (tok < TINY.vocab)).all()
 
 
+def test_models_with_different_stages_interleave() -> None:
+    """Two models of one process whose kernels need different shared-memory stages (1 and 8 rows) step in
+    turn: the kernel's allowance is raised for the larger one and never lowered for the smaller one."""
+    w = synth.make_weights(TINY, seed=6)
+    small = _core.init_model(synth.metadata_of(w), capacity=64)
+    big = _core.init_model(synth.metadata_of(w), max_batch=8, capacity=64)
+    small2 = _core.init_model(synth.metadata_of(w), capacity=64)
+    ref = oracle.RefModel(w, max_seq_len=64)
+    for t in synth.prompt_ids(4, TINY.vocab, seed=2):
+        want = ref.step(int(t))
+        close_logits(_core.step(small, int(t), 0.0, 0, 1.0), want)
+        lg, _tok = _core.step_rows(big, [int(t)] * 8, sampling=(0.0, 0, 1.0))
+        close_logits(lg[7], want)
+        close_logits(_core.step(small2, int(t), 0.0, 0, 1.0), want)
+    for m in (small, big, small2):
+        m["_handle"].close()
+
+
+def _split_phases(d: synth.Gemma3Dims, esz: int, ctas: int) -> set[str]:
+    """Phases whose row groups the kernel splits between two CTAs: the tile shape and the rule of gemv_geom."""
+    out = set()
+    if esz == 4:
+        return out  # only the bf16 kernels split
+    hp, ip, ap = (-(-k // 128) * 128 for k in (d.hidden, d.intermediate, d.heads * d.head_dim))
+    for name, n, kp, pair in (("QKV", (d.heads + 2 * d.kv_heads) * d.head_dim, hp, False), ("O", d.hidden, ap, False),
+                              ("GU", d.intermediate, hp, True), ("D", d.hidden, ip, False)):
+        rps = 8 * (2 if esz == 2 else 1)
+        nseg = max(1, -(-kp * rps * (2 if pair else 1) * esz // 36864))
+        while kp % nseg or (kp // nseg) % 8:
+            nseg += 1
+        groups = -(-n // rps)
+        units = groups * nseg
+        if nseg > 1 and units // ctas >= nseg and -(-groups // ctas) * nseg - -(-units // ctas) >= 2:
+            out.add(name)
+    return out
+
+
+@pytest.mark.parametrize(("hidden", "inter", "bf16", "want"),
+                         [(1536, 2560, True, {"GU"}), (2560, 4096, True, {"D"}), (1280, 4096, False, set())])
+def test_split_row_groups_match_oracle(monkeypatch, hidden: int, inter: int, bf16: bool, want: set) -> None:
+    """bf16 shapes whose whole row groups leave some CTAs two or more tiles above the even share (as
+    Gemma3-4B's down_proj: 160 groups on 148 CTAs) split the (group, segment) tiles evenly; the two CTAs of
+    a split group add their partial sums.  Logits at 1 and 3 rows match the oracle, with and without the
+    split; the fp32 kernels never split."""
+    import torch  # noqa: PLC0415
+
+    d = synth.tiny(hidden=hidden, layers=2, heads=4, kv_heads=1, head_dim=256, intermediate=inter, vocab=2048)
+    assert _split_phases(d, 2 if bf16 else 4, torch.cuda.get_device_properties(0).multi_processor_count) == want
+    w = synth.make_weights(d, seed=8, bf16=bf16)
+    wd = "bf16" if bf16 else "f32"
+    rows = [[int(t) for t in synth.prompt_ids(n, d.vocab, seed=60 + n)] for n in (5, 9, 3)]
+    for split in ("1", "0"):
+        monkeypatch.setenv("MOGEMMA_B200_SPLIT", split)
+        one = _core.init_model(synth.metadata_of(w), capacity=64, weight_dtype=wd)
+        three = _core.init_model(synth.metadata_of(w), max_batch=3, capacity=64, weight_dtype=wd)
+        ref = oracle.RefModel(w, max_seq_len=64)
+        for t in rows[1]:
+            close_logits(_core.step(one, t, 0.0, 0, 1.0), ref.step(t))
+        _core.prefill_rows(three, [r[:-1] for r in rows])
+        lg, _tok = _core.step_rows(three, [r[-1] for r in rows], sampling=(0.0, 0, 1.0))
+        for i, r in enumerate(rows):
+            ref = oracle.RefModel(w, max_seq_len=64)
+            for t in r[:-1]:
+                ref.step_no_logits(t)
+            close_logits(lg[i], ref.step(r[-1]))
+        one["_handle"].close()
+        three["_handle"].close()
+
+
 @pytest.mark.parametrize("params", [(0.0, 50, 1.0), (0.7, 64, 1.0), (0.7, 10, 0.9), (1.0, 3, 1.0)])
 def test_fused_draw_matches_rules_on_device_logits(params: tuple[float, int, float]) -> None:
     w, llm = build(TINY)
