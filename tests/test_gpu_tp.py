@@ -38,12 +38,13 @@ def _free_port() -> int:
         return int(s.getsockname()[1])
 
 
-def _run(tmp_path: Path, ranks: int, kv_heads: int, heads: int = 4, head_dim: int = 64) -> None:
+def _run(tmp_path: Path, ranks: int, kv_heads: int, heads: int = 4, head_dim: int = 64, extra: tuple = ()) -> None:
     out = tmp_path / "tp.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={ranks}",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(ROOT / "tests" / "tp_worker.py"),
-           "--out", str(out), "--kv-heads", str(kv_heads), "--heads", str(heads), "--head-dim", str(head_dim)]
+           "--out", str(out), "--kv-heads", str(kv_heads), "--heads", str(heads), "--head-dim", str(head_dim),
+           *extra]
     proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600, check=False)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
     res = json.loads(out.read_text())
@@ -64,3 +65,13 @@ def test_tensor_parallel_27b_head_geometry(tmp_path: Path, ranks: int) -> None:
     if _gpus() < ranks:
         pytest.skip(f"needs {ranks} GPUs")
     _run(tmp_path, ranks, kv_heads=8, heads=16, head_dim=128)
+
+
+def test_tensor_parallel_split_row_groups(tmp_path: Path) -> None:
+    """bf16 hidden 2560, FFN 8192 over 2 ranks: each rank's down_proj has 160 row groups of 4 tiles for 148
+    CTAs, so its tiles are split evenly and the CTAs that share a group add their partial sums before the rows
+    go to every rank's exchange buffer."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run(tmp_path, 2, kv_heads=2, heads=4, head_dim=256,
+         extra=("--hidden", "2560", "--intermediate", "8192", "--bf16"))

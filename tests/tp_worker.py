@@ -35,6 +35,9 @@ def main() -> int:
     ap.add_argument("--heads", type=int, default=4)
     ap.add_argument("--head-dim", type=int, default=64)
     ap.add_argument("--steps", type=int, default=12)
+    ap.add_argument("--hidden", type=int, default=256)
+    ap.add_argument("--intermediate", type=int, default=512)
+    ap.add_argument("--bf16", action="store_true", help="bf16 weights (the kernels that split row groups)")
     args = ap.parse_args()
 
     import torch
@@ -46,10 +49,12 @@ def main() -> int:
     world = int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
-    d = synth.tiny(heads=args.heads, kv_heads=args.kv_heads, head_dim=args.head_dim, intermediate=512, vocab=4096)
-    w = synth.make_weights(d, seed=11)
+    d = synth.tiny(hidden=args.hidden, heads=args.heads, kv_heads=args.kv_heads, head_dim=args.head_dim,
+                   intermediate=args.intermediate, vocab=4096)
+    w = synth.make_weights(d, seed=11, bf16=args.bf16)
     meta = synth.metadata_of(w)
-    llm = _core.init_model_tp(meta, device=rank, capacity=64, seed=7)
+    wd = "bf16" if args.bf16 else "f32"
+    llm = _core.init_model_tp(meta, device=rank, capacity=64, seed=7, weight_dtype=wd)
     toks = [int(t) for t in synth.prompt_ids(args.steps, d.vocab, seed=5)]
     result: dict = {"world": world, "kv_heads": args.kv_heads, "heads": args.heads, "head_dim": args.head_dim}
 
@@ -77,7 +82,7 @@ def main() -> int:
             r = ref.step(t)
             errs.append(float(np.max(np.abs(lg - r))) / (LOGIT_ATOL + LOGIT_RTOL * float(np.max(np.abs(r)))))
         result["oracle_err_over_tol"] = max(errs)
-        single = _core.init_model(meta, device=0, capacity=64, seed=7)
+        single = _core.init_model(meta, device=0, capacity=64, seed=7, weight_dtype=wd)
         one_logits, one_greedy, _ = run(single)
         result["single_gpu_max_abs_diff"] = max(float(np.max(np.abs(a - b))) for a, b in zip(one_logits, tp_logits))
         result["greedy_equal_single_gpu"] = one_greedy == greedy
