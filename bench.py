@@ -426,7 +426,7 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled before the timed decode")
     ap.add_argument("--decode", type=int, default=DECODE, help="tokens decoded per step")
     ap.add_argument("--batch", type=int, default=1,
-                    help="decode rows (beyond the persistent kernel's 8 rows: one launch per group of 8 rows, "
+                    help="decode rows (beyond the rows one persistent launch holds: one launch per row group, "
                          "or the batched tensor-core steps with --batched-tc)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "embed"],
                     help="prefill: the batched tensor-core prefill of --prompt tokens; embed: the bidirectional "
@@ -522,8 +522,9 @@ def main() -> None:
     tokens = args.steps * DECODE * streams * B
     value = tokens / (ms / 1000.0)
     ms_launch = ms / (args.steps * DECODE)
-    tc_path = B > 8 and args.batched_tc and not tp
-    groups = -(-B // 8)  # decode-kernel launches per token: one per group of up to 8 rows
+    rows = h.rows_per_launch  # rows one decode launch holds (4 for Gemma3-1B fp32: the down_proj input stage)
+    tc_path = B > rows and args.batched_tc and not tp
+    groups = -(-B // rows)  # decode-kernel launches per token
     bytes_launch = algorithmic_bytes(info, PROMPT - 1, DECODE, B, bf16_copies=tc_path)
     achieved = bytes_launch / (ms_launch / 1000.0) / 1e9
     pk = peaks()
@@ -568,16 +569,17 @@ def main() -> None:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"],
                          "traffic": (bytes_launch * TRAFFIC_RATIO[(CONFIG, args.weight_dtype)]
-                                     if (CONFIG, args.weight_dtype) in TRAFFIC_RATIO and B <= 8 else None),
+                                     if (CONFIG, args.weight_dtype) in TRAFFIC_RATIO and B <= rows else None),
                          "traffic_source": "ncu dram__bytes_read+write of a Gemma3-270M launch, scaled by bytes",
                          "peak_source": pk["source"],
                          "kernel": ("batched step: tcgen05 GEMMs + prefill kernels per layer, lm_head GEMM, sampler"
-                                    if tc_path else "decode_kernel (one launch per token)" if B <= 8 else
-                                    f"decode_kernel (one launch per token per group of 8 rows: {groups})"),
+                                    if tc_path else "decode_kernel (one launch per token)" if B <= rows else
+                                    f"decode_kernel ({groups} launches of up to {rows} rows per token)"),
                          "algorithmic_bytes_per_launch": bytes_launch},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
             "gpu_launches": args.steps * DECODE * (9 * d.layers + 4 if tc_path else groups),
+            "rows_per_launch": rows,
             "ms_per_token": ms_launch,
         }
         print(json.dumps(line), flush=True)

@@ -131,6 +131,12 @@ mg_status mg_model_info_get(const mg_model *m, mg_model_info *info);
 mg_status mg_model_destroy(mg_model *m);
 /* The cudaStream_t the model runs on (for event timing by the caller). */
 void *mg_model_stream(const mg_model *m);
+/* Rows one persistent decode launch holds for this model: the input stage of
+ * the widest projection (down_proj: intermediate_size floats per row) must fit
+ * in shared memory beside the weight ring, so it is at most 8 and fewer for
+ * wide FFNs (4 for Gemma3-1B fp32).  Steps with more rows run one launch per
+ * group of this many rows.  0 for a NULL model. */
+int32_t mg_rows_per_launch(const mg_model *m);
 
 /* ---- positions (per batch row) ---- */
 mg_status mg_set_pos(mg_model *m, int32_t row, int32_t pos); /* row -1: every row */

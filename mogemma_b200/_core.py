@@ -119,6 +119,8 @@ _lib.mg_model_info_get.argtypes = [_P, ctypes.POINTER(ModelInfo)]
 _lib.mg_model_destroy.argtypes = [_P]
 _lib.mg_model_stream.argtypes = [_P]
 _lib.mg_model_stream.restype = _P
+_lib.mg_rows_per_launch.argtypes = [_P]
+_lib.mg_rows_per_launch.restype = ctypes.c_int32
 _lib.mg_set_pos.argtypes = [_P, ctypes.c_int32, ctypes.c_int32]
 _lib.mg_get_pos.argtypes = [_P, _I32P, ctypes.c_int32]
 _lib.mg_step.argtypes = [_P, _I32P, ctypes.c_int32, _F32P, _I32P, ctypes.POINTER(Sampling)]
@@ -191,6 +193,11 @@ class ModelHandle:
     @property
     def stream(self) -> int:
         return int(_lib.mg_model_stream(self.ptr) or 0)
+
+    @property
+    def rows_per_launch(self) -> int:
+        """Rows one persistent decode launch holds (more rows run one launch per group)."""
+        return int(_lib.mg_rows_per_launch(self.ptr))
 
     def set_pos(self, pos: int, row: int = -1) -> None:
         _check(_lib.mg_set_pos(self.ptr, row, int(pos)))

@@ -804,6 +804,8 @@ extern "C" mg_status mg_model_create(const mg_tensor_desc *descs, int32_t n, con
     return MG_OK;
 }
 
+extern "C" int32_t mg_rows_per_launch(const mg_model *m) { return m ? m->Bdec : 0; }
+
 extern "C" mg_status mg_model_info_get(const mg_model *m, mg_model_info *info) {
     if (!m || !info) return fail(MG_ERR_INVALID, "null argument");
     info->num_layers = m->L;

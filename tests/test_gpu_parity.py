@@ -140,6 +140,7 @@ def test_rows_beyond_the_kernel_rows_in_fp32() -> None:
     """12 rows on a model created with prefill_path 0: the decode kernel runs one launch per row group
     (8 + 4 rows), each row in the reference's fp32 arithmetic at its own position."""
     w, llm = build(TINY, max_batch=12, capacity=64)
+    assert 1 <= llm["_handle"].rows_per_launch <= 8
     rows = [[int(t) for t in synth.prompt_ids(3 + 2 * i, TINY.vocab, seed=50 + i)] for i in range(12)]
     _core.prefill_rows(llm, [r[:-1] for r in rows])
     assert llm["_handle"].get_pos()[:12] == [len(r) - 1 for r in rows]
