@@ -522,9 +522,9 @@ def main() -> None:
     tokens = args.steps * DECODE * streams * B
     value = tokens / (ms / 1000.0)
     ms_launch = ms / (args.steps * DECODE)
-    rows = h.rows_per_launch  # rows one decode launch holds (4 for Gemma3-1B fp32: the down_proj input stage)
+    rows = h.rows_per_launch  # rows one decode launch holds (5 for Gemma3-1B fp32: the down_proj input stage)
     tc_path = B > rows and args.batched_tc and not tp
-    groups = -(-B // rows)  # decode-kernel launches per token
+    groups = -(-B // rows)  # decode-kernel launches per token (equal groups of at most `rows`)
     bytes_launch = algorithmic_bytes(info, PROMPT - 1, DECODE, B, bf16_copies=tc_path)
     achieved = bytes_launch / (ms_launch / 1000.0) / 1e9
     pk = peaks()

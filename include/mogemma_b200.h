@@ -134,8 +134,8 @@ void *mg_model_stream(const mg_model *m);
 /* Rows one persistent decode launch holds for this model: the input stage of
  * the widest projection (down_proj: intermediate_size floats per row) must fit
  * in shared memory beside the weight ring, so it is at most 8 and fewer for
- * wide FFNs (4 for Gemma3-1B fp32).  Steps with more rows run one launch per
- * group of this many rows.  0 for a NULL model. */
+ * wide FFNs (5 for Gemma3-1B fp32).  Steps with more rows run as few launches
+ * as this allows, of equal size.  0 for a NULL model. */
 int32_t mg_rows_per_launch(const mg_model *m);
 
 /* ---- positions (per batch row) ---- */

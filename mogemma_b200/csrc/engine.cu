@@ -198,6 +198,10 @@ struct mg_model {
     // rows: Bmax in the KV cache; Bdec the most the persistent decode kernel
     // stages (shared memory); steps with more rows take the batched path
     int Bdec = 1, nrows = kMaxRows;
+    // per launch row count b (1..Bdec): its activation stage, ring stages and
+    // dynamic shared memory -- fewer rows leave room for a deeper ring
+    int S_rows[kMaxRows + 1] = {}, xs_rows[kMaxRows + 1] = {};
+    size_t smem_rows[kMaxRows + 1] = {};
 };
 
 static int split_kinds(const mg_model *m);
@@ -547,6 +551,19 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
                     "models run one launch of rows",
                     m->Bmax, m->Bdec);
     m->smem = decode_smem_bytes(m->S, m->xs_floats, L);
+    for (int b = 1; b <= m->Bdec; ++b) {
+        m->xs_rows[b] = stage_floats(b);
+        m->S_rows[b] = m->S;
+        m->smem_rows[b] = m->smem;
+        for (int S = 8; S > m->S; --S)
+            if (decode_smem_bytes(S, m->xs_rows[b], L) + static_smem <= static_cast<size_t>(max_smem)) {
+                m->S_rows[b] = S;
+                break;
+            }
+        if (m->S_rows[b] == m->S) m->xs_rows[b] = m->xs_floats;  // the full-width layout
+        m->smem_rows[b] = decode_smem_bytes(m->S_rows[b], m->xs_rows[b], L);
+        m->smem = std::max(m->smem, m->smem_rows[b]);  // the kernel's allowance covers every launch
+    }
     if (m->wdtype == MG_F32) {
         CU(decode_prepare<float>(m->smem));
     } else {
@@ -958,18 +975,23 @@ static mg_status run_decode(mg_model *m, DecodeParams &p, int max_ctx) {
         m->epoch = 1;
     }
     p.epoch = m->epoch;
+    // the ring depth and stage of this launch's row count
+    const int rb = std::min(std::max(p.B, 1), m->Bdec);
+    p.S = m->S_rows[rb];
+    p.xs_floats = m->xs_rows[rb];
+    const size_t smem = m->smem_rows[rb];
     const bool persistent = m->decode_path == 0;
     if (persistent) {
-        cudaError_t e = m->wdtype == MG_F32 ? decode_launch<float>(p, m->G, m->smem, m->stream, true)
-                                            : decode_launch<__nv_bfloat16>(p, m->G, m->smem, m->stream, true);
+        cudaError_t e = m->wdtype == MG_F32 ? decode_launch<float>(p, m->G, smem, m->stream, true)
+                                            : decode_launch<__nv_bfloat16>(p, m->G, smem, m->stream, true);
         if (e != cudaSuccess) return fail(MG_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
     } else {
         for (int ph = 0; ph < p.n_phases; ++ph) {
             DecodeParams q = p;
             q.ph_begin = ph;
             q.ph_end = ph + 1;
-            cudaError_t e = m->wdtype == MG_F32 ? decode_launch<float>(q, m->G, m->smem, m->stream, false)
-                                                : decode_launch<__nv_bfloat16>(q, m->G, m->smem, m->stream, false);
+            cudaError_t e = m->wdtype == MG_F32 ? decode_launch<float>(q, m->G, smem, m->stream, false)
+                                                : decode_launch<__nv_bfloat16>(q, m->G, smem, m->stream, false);
             if (e != cudaSuccess) return fail(MG_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
         }
     }
@@ -1060,8 +1082,12 @@ static void row_window(const mg_model *m, DecodeParams &p, int r0, int nb) {
 // persistent kernel holds them all, else one per row group.  `p` is a template
 // for rows [0, batch) (lm_mode, sampling, out_tokens, uniforms, ids set).
 static mg_status run_rows(mg_model *m, const DecodeParams &p, int batch, const std::vector<int> &ctx) {
-    for (int r0 = 0; r0 < batch; r0 += m->Bdec) {
-        const int nb = std::min(m->Bdec, batch - r0);
+    // as few launches as the row limit allows, of equal size (16 rows at a limit of 5: four launches of 4
+    // rows, each with the deeper ring of 4 rows)
+    const int ngroups = (batch + m->Bdec - 1) / m->Bdec;
+    const int per = (batch + ngroups - 1) / ngroups;
+    for (int r0 = 0; r0 < batch; r0 += per) {
+        const int nb = std::min(per, batch - r0);
         DecodeParams q = p;
         if (batch > m->Bdec) row_window(m, q, r0, nb);
         int max_ctx = 0;

@@ -138,7 +138,8 @@ def test_batched_rows_match_independent_runs() -> None:
 
 def test_rows_beyond_the_kernel_rows_in_fp32() -> None:
     """12 rows on a model created with prefill_path 0: the decode kernel runs one launch per row group
-    (8 + 4 rows), each row in the reference's fp32 arithmetic at its own position."""
+    (two launches of 6 rows when a launch holds 8), each row in the reference's fp32 arithmetic at its own
+    position."""
     w, llm = build(TINY, max_batch=12, capacity=64)
     assert 1 <= llm["_handle"].rows_per_launch <= 8
     rows = [[int(t) for t in synth.prompt_ids(3 + 2 * i, TINY.vocab, seed=50 + i)] for i in range(12)]
