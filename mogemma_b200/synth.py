@@ -111,6 +111,100 @@ def make_weights(d: Gemma3Dims, *, seed: int = 0, std: float = 0.02, bf16: bool 
     return out
 
 
+@dataclass(frozen=True)
+class NanoDims:
+    """Gemma 3n ("nano") shapes.  ``kv_share_start``: layers from here on carry zero k/v projections
+    and read an earlier layer's cache (src/mo/mogemma/core.mojo:261-273); ``table_layers``: the
+    per-layer embedding table's layer count (defaults to ``layers``)."""
+
+    name: str
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    per_layer_dim: int
+    laurel_rank: int
+    modalities: int = 4
+    vocab: int = 262144
+    kv_share_start: int | None = None
+    table_layers: int | None = None
+
+
+def nano_tiny(hidden: int = 64, layers: int = 12, heads: int = 4, kv_heads: int = 2, head_dim: int = 16,
+              intermediate: int = 96, per_layer_dim: int = 8, laurel_rank: int = 8, vocab: int = 512,
+              kv_share_start: int | None = 8, table_layers: int | None = None) -> NanoDims:
+    """A small Gemma 3n configuration for oracle-speed tests (12 layers: sparse and dense MLPs, both
+    attention kinds, KV sharing from layer 8)."""
+    return NanoDims("nano-tiny", hidden, layers, heads, kv_heads, head_dim, intermediate, per_layer_dim, laurel_rank,
+                    4, vocab, kv_share_start, table_layers)
+
+
+def nano_tensor_shapes(d: NanoDims) -> dict[str, tuple[int, ...]]:
+    """Tensor names and shapes the reference's nano loader reads (src/mo/mogemma/core.mojo:111-165)."""
+    H, P, T, nm = d.hidden, d.per_layer_dim, d.table_layers or d.layers, d.modalities
+    q, kv = d.heads * d.head_dim, d.kv_heads * d.head_dim
+    shapes: dict[str, tuple[int, ...]] = {
+        "model.embed_tokens.weight": (d.vocab, H),
+        "model.norm.weight": (H,),
+        "model.per_layer_embed.weight": (d.vocab, T, P),
+        "model.per_layer_embed.projection.weight": (H, T, P),
+        "model.per_layer_embed.norm.weight": (P,),
+    }
+    for i in range(nm - 1):
+        shapes[f"model.altup.projection.{i}.weight"] = (H, H)
+        shapes[f"model.altup.unembed.{i}.weight"] = (H, H)
+    for i in range(d.layers):
+        p = f"model.layers.{i}."
+        for n in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                  "post_feedforward_layernorm"):
+            shapes[p + n + ".weight"] = (H,)
+        shapes[p + "self_attn.q_proj.weight"] = (q, H)
+        shapes[p + "self_attn.k_proj.weight"] = (kv, H)
+        shapes[p + "self_attn.v_proj.weight"] = (kv, H)
+        shapes[p + "self_attn.o_proj.weight"] = (H, q)
+        shapes[p + "self_attn.q_norm.weight"] = (d.head_dim,)
+        shapes[p + "self_attn.k_norm.weight"] = (d.head_dim,)
+        shapes[p + "mlp.gate_proj.weight"] = (d.intermediate, H)
+        shapes[p + "mlp.up_proj.weight"] = (d.intermediate, H)
+        shapes[p + "mlp.down_proj.weight"] = (H, d.intermediate)
+        shapes[p + "altup.router.weight"] = (nm, H)
+        shapes[p + "altup.router_norm.weight"] = (H,)
+        shapes[p + "altup.prediction_coefs"] = (nm, nm, nm)
+        shapes[p + "altup.correction_coefs"] = (nm, nm)
+        shapes[p + "altup.output_scale"] = (H,)
+        shapes[p + "laurel.down_proj.weight"] = (d.laurel_rank, H)
+        shapes[p + "laurel.up_proj.weight"] = (H, d.laurel_rank)
+        shapes[p + "laurel.norm.weight"] = (H,)
+        shapes[p + "per_layer_map.gate.weight"] = (P, H)
+        shapes[p + "per_layer_map.projection.weight"] = (H, P)
+        shapes[p + "per_layer_map.norm.weight"] = (H,)
+    return shapes
+
+
+def make_nano_weights(d: NanoDims, *, seed: int = 0, std: float = 0.02,
+                      scales: dict[str, float] | None = None) -> dict[str, np.ndarray]:
+    """Seeded Gemma 3n weights: N(0, std) matrices, norm weights and AltUp output scales 1 + N(0, std)
+    (the nano norms multiply by the weight itself), k/v projections of layers from kv_share_start on
+    zero; ``lm_head.weight`` aliases the embedding.  ``scales`` multiplies the noise of tensors whose
+    name contains a key (e.g. larger AltUp coefficients)."""
+    out: dict[str, np.ndarray] = {}
+    for name, shape in nano_tensor_shapes(d).items():
+        rng = np.random.default_rng(_subseed(seed, name))
+        k = np.float32(std * next((v for key, v in (scales or {}).items() if key in name), 1.0))
+        a = rng.standard_normal(shape, dtype=np.float32) * k
+        if name.endswith("norm.weight") or name.endswith("output_scale"):
+            a += np.float32(1.0)
+        layer = int(name.split(".")[2]) if name.startswith("model.layers.") else -1
+        if d.kv_share_start is not None and layer >= d.kv_share_start and (
+                name.endswith("k_proj.weight") or name.endswith("v_proj.weight")):
+            a[...] = 0.0
+        out[name] = a
+    out["lm_head.weight"] = out["model.embed_tokens.weight"]
+    return out
+
+
 def metadata_of(weights: dict[str, np.ndarray]) -> dict[str, tuple[int, tuple[int, ...], str]]:
     """Loader-style ``{name: (ptr, shape, dtype)}`` over in-memory arrays."""
     return {k: (int(v.ctypes.data), tuple(v.shape), "F32") for k, v in weights.items()}
