@@ -261,6 +261,39 @@ mg_status mg_gemm_bf16(const void *a_dev, int64_t lda, const void *b_dev, int64_
  * before any rank destroys its model, so no buffer is freed while mapped. */
 mg_status mg_tp_disconnect(mg_model *m);
 
+/* ---- Gemma 3n ("nano") decode ----
+ * The reference switches to its nano graph when the checkpoint has AltUp
+ * routers (src/mo/mogemma/core.mojo:26-31) and runs forward_nano_step
+ * (src/mo/mogemma/layers.mojo:959-1004) per token.  mg_nano_create takes the
+ * tensors the reference's nano loader reads (core.mojo:111-165: embedding,
+ * final norm, lm_head, per_layer_embed{,.projection,.norm},
+ * altup.{projection,unembed}.i, and per layer the base, altup, laurel and
+ * per_layer_map tensors), fp32 or bf16 (widened to fp32), and a position
+ * capacity.  Dimensions, the AltUp stream count and the KV-sharing start are
+ * inferred as init_model_mojo does (core.mojo:296-312, 261-273).  One decode
+ * step is a CUDA graph replayed per token. */
+typedef struct mg_nano mg_nano;
+typedef struct mg_nano_info {
+    int32_t num_layers, num_heads, num_kv_heads, head_dim;
+    int32_t hidden_size, intermediate_size, vocab_size, per_layer_dim;
+    int32_t modalities, laurel_rank, kv_share_start, max_seq_len;
+} mg_nano_info;
+mg_status mg_nano_create(const mg_tensor_desc *descs, int32_t n, int32_t device, int32_t capacity, mg_nano **out);
+mg_status mg_nano_info_get(const mg_nano *m, mg_nano_info *info);
+mg_status mg_nano_destroy(mg_nano *m);
+mg_status mg_nano_set_pos(mg_nano *m, int32_t pos);
+mg_status mg_nano_get_pos(const mg_nano *m, int32_t *pos);
+/* step_mojo for arch "nano" (core.mojo:366-461): the token at the model's
+ * position, logits_host (nullable: no lm_head) gets [vocab] fp32 logits,
+ * the position advances; MG_ERR_SEQ_EXCEEDED at capacity. */
+mg_status mg_nano_step(mg_nano *m, int32_t token_id, float *logits_host);
+/* The prefill loop of model.py:344-345 (steps without logits). */
+mg_status mg_nano_prefill(mg_nano *m, const int32_t *ids, int32_t n);
+/* forward_nano_sequence (layers.mojo:1007-1063): mean of the final hidden
+ * states of tokens 0..n-1 (the model's KV rows 0..n-1 serve as scratch; its
+ * position is restored). */
+mg_status mg_nano_embed(mg_nano *m, const int32_t *ids, int32_t n, float *out_host);
+
 #ifdef __cplusplus
 }
 #endif

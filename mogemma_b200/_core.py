@@ -107,6 +107,12 @@ class Sampling(ctypes.Structure):
     ]
 
 
+class NanoInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "num_layers", "num_heads", "num_kv_heads", "head_dim", "hidden_size", "intermediate_size", "vocab_size",
+        "per_layer_dim", "modalities", "laurel_rank", "kv_share_start", "max_seq_len")]
+
+
 _P = ctypes.c_void_p
 _I32P = ctypes.POINTER(ctypes.c_int32)
 _F32P = ctypes.POINTER(ctypes.c_float)
@@ -121,6 +127,15 @@ _lib.mg_model_stream.argtypes = [_P]
 _lib.mg_model_stream.restype = _P
 _lib.mg_rows_per_launch.argtypes = [_P]
 _lib.mg_rows_per_launch.restype = ctypes.c_int32
+_lib.mg_nano_create.argtypes = [ctypes.POINTER(TensorDesc), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                ctypes.POINTER(_P)]
+_lib.mg_nano_info_get.argtypes = [_P, ctypes.POINTER(NanoInfo)]
+_lib.mg_nano_destroy.argtypes = [_P]
+_lib.mg_nano_set_pos.argtypes = [_P, ctypes.c_int32]
+_lib.mg_nano_get_pos.argtypes = [_P, _I32P]
+_lib.mg_nano_step.argtypes = [_P, ctypes.c_int32, _F32P]
+_lib.mg_nano_prefill.argtypes = [_P, _I32P, ctypes.c_int32]
+_lib.mg_nano_embed.argtypes = [_P, _I32P, ctypes.c_int32, _F32P]
 _lib.mg_set_pos.argtypes = [_P, ctypes.c_int32, ctypes.c_int32]
 _lib.mg_get_pos.argtypes = [_P, _I32P, ctypes.c_int32]
 _lib.mg_step.argtypes = [_P, _I32P, ctypes.c_int32, _F32P, _I32P, ctypes.POINTER(Sampling)]
@@ -307,6 +322,100 @@ def create_model(metadata: dict[str, Any], **options: Any) -> ModelHandle:
     return ModelHandle(int(out.value), info)
 
 
+class NanoHandle:
+    """Owns one ``mg_nano`` (Gemma 3n decode engine)."""
+
+    def __init__(self, ptr: int, info: NanoInfo) -> None:
+        self.ptr = ptr
+        self.info = info
+        self.pos = 0
+
+    def close(self) -> None:
+        if self.ptr:
+            _lib.mg_nano_destroy(self.ptr)
+            self.ptr = 0
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+    def set_pos(self, pos: int) -> None:
+        _check(_lib.mg_nano_set_pos(self.ptr, int(pos)))
+        self.pos = int(pos)
+
+
+def _tensor_descs(metadata: dict[str, Any]) -> tuple[Any, list[bytes]]:
+    names = list(metadata.keys())
+    descs = (TensorDesc * len(names))()
+    keep: list[bytes] = []
+    for i, name in enumerate(names):
+        meta = metadata[name]
+        ptr, shape = int(meta[0]), tuple(int(s) for s in meta[1])
+        dtype = str(meta[2]) if len(meta) > 2 else "F32"
+        nb = name.encode()
+        keep.append(nb)
+        descs[i].name = nb
+        descs[i].data = ptr
+        descs[i].ndim = min(len(shape), 4)
+        for k in range(descs[i].ndim):
+            descs[i].shape[k] = shape[k]
+        descs[i].dtype = _DTYPES.get(dtype.upper(), MG_OTHER)
+    return descs, keep
+
+
+def create_nano(metadata: dict[str, Any], **options: Any) -> NanoHandle:
+    """``mg_nano_create`` over loader metadata of a Gemma 3n checkpoint."""
+    descs, _keep = _tensor_descs(metadata)
+    device = int(options.get("device", _env_int("MOGEMMA_B200_DEVICE", 0)))
+    capacity = int(options.get("capacity", _env_int("MOGEMMA_B200_CAPACITY", 8192)))
+    out = _P()
+    _check(_lib.mg_nano_create(descs, len(descs), device, capacity, ctypes.byref(out)))
+    info = NanoInfo()
+    _check(_lib.mg_nano_info_get(out, ctypes.byref(info)))
+    return NanoHandle(int(out.value), info)
+
+
+def _init_nano(metadata: dict[str, Any], **options: Any) -> dict[str, Any]:
+    """init_model_mojo's nano branch (core.mojo:296-312, 350-364)."""
+    handle = create_nano(metadata, **options)
+    info = handle.info
+    runtime = {k: metadata.get(v) for k, v in (
+        ("embed_tokens", "model.embed_tokens.weight"), ("norm", "model.norm.weight"), ("lm_head", "lm_head.weight"),
+        ("per_layer_embed", "model.per_layer_embed.weight"))}
+    return {
+        "engine": ENGINE_NAME,
+        "arch": "nano",
+        "max_seq_len": int(info.max_seq_len),
+        "num_layers": int(info.num_layers),
+        "num_kv_heads": int(info.num_kv_heads),
+        "head_dim": int(info.head_dim),
+        "hidden_size": int(info.hidden_size),
+        "intermediate_size": int(info.intermediate_size),
+        "vocab_size": int(info.vocab_size),
+        "per_layer_dim": int(info.per_layer_dim),
+        "kv_share_start": int(info.kv_share_start),
+        "runtime": runtime,
+        "pos": 0,
+        "_handle": handle,
+    }
+
+
+def _nano(llm: dict[str, Any]) -> NanoHandle | None:
+    """The Gemma 3n handle of ``llm`` (position synced from ``llm["pos"]``), or None."""
+    h = llm.get("_handle")
+    if not isinstance(h, NanoHandle):
+        return None
+    if not h.ptr:
+        msg = "llm was closed"
+        raise RuntimeError(msg)
+    pos = int(llm.get("pos", 0))
+    if pos != h.pos:
+        h.set_pos(pos)
+    return h
+
+
 # ------------------------------------------------------------- reference API
 def init_model(metadata: dict[str, Any], **options: Any) -> dict[str, Any]:
     """Reference ``init_model`` (core.mojo:274-364): returns the ``llm`` dict.
@@ -315,9 +424,8 @@ def init_model(metadata: dict[str, Any], **options: Any) -> dict[str, Any]:
     Extra keyword options (mode, weight_dtype, max_batch, capacity, device,
     seed, decode_path, ...) are private to this engine.
     """
-    if "model.layers.0.altup.router.weight" in metadata:
-        msg = "Gemma 3n (nano) checkpoints are not supported by the B200 engine"
-        raise RuntimeError(msg)
+    if "model.layers.0.altup.router.weight" in metadata:  # core.mojo:26-31: arch "nano"
+        return _init_nano(metadata, **options)
     handle = create_model(metadata, **options)
     info = handle.info
     runtime = {
@@ -383,6 +491,10 @@ def close_tp(llm: dict[str, Any], group: Any = None) -> None:
 
 def _handle(llm: dict[str, Any]) -> ModelHandle:
     h = llm.get("_handle")
+    if isinstance(h, NanoHandle):
+        msg = "this call is not available for Gemma 3n (nano) models: use init_model / step / prefill / " \
+              "step_sample / generate_embeddings"
+        raise RuntimeError(msg)
     if not isinstance(h, ModelHandle) or not h.ptr:
         msg = "llm was not created by mogemma_b200._core.init_model"
         raise RuntimeError(msg)
@@ -397,6 +509,15 @@ def step(llm: dict[str, Any], token_id: int, temperature: float, top_k: int, top
     fp32 logits of shape (vocab,) and advances ``llm["pos"]``.  The sampling
     arguments are accepted and unused, as in the reference."""
     del temperature, top_k, top_p
+    nh = _nano(llm)
+    if nh is not None:
+        if nh.pos >= int(llm["max_seq_len"]):
+            raise RuntimeError("Sequence length exceeded")
+        logits = np.empty(int(llm["vocab_size"]), dtype=np.float32)
+        _check(_lib.mg_nano_step(nh.ptr, int(token_id), logits.ctypes.data_as(_F32P)))
+        nh.pos += 1
+        llm["pos"] = nh.pos
+        return logits
     h = _handle(llm)
     if h.pos >= int(llm["max_seq_len"]):
         raise RuntimeError("Sequence length exceeded")
@@ -411,7 +532,15 @@ def step(llm: dict[str, Any], token_id: int, temperature: float, top_k: int, top
 def step_sample(llm: dict[str, Any], token_id: int, temperature: float, top_k: int, top_p: float,
                 uniform: float | None = None) -> int:
     """One decode step with the draw of ``_sample_next_token`` done on device;
-    returns the sampled token id (4 bytes cross the bus instead of the logits)."""
+    returns the sampled token id (4 bytes cross the bus instead of the logits).
+    Gemma 3n models return their logits to the host and draw with ``sample``
+    (Philox stream keyed by the model's seed option and the position)."""
+    nh = _nano(llm)
+    if nh is not None:
+        pos = nh.pos
+        logits = step(llm, token_id, temperature, top_k, top_p)
+        return int(sample(logits, temperature, top_k, top_p, seed=int(llm.get("seed", 0)), offset=pos,
+                          uniforms=None if uniform is None else [uniform])[0])
     h = _handle(llm)
     if h.pos >= int(llm["max_seq_len"]):
         raise RuntimeError("Sequence length exceeded")
@@ -484,6 +613,14 @@ def prefill(llm: dict[str, Any], tokens: Sequence[int]) -> None:
     toks = _i32(list(tokens))
     if toks.size == 0:
         return
+    nh = _nano(llm)
+    if nh is not None:
+        if nh.pos + toks.size > int(llm["max_seq_len"]):
+            raise RuntimeError("Sequence length exceeded")
+        _check(_lib.mg_nano_prefill(nh.ptr, toks.ctypes.data_as(_I32P), int(toks.size)))
+        nh.pos += int(toks.size)
+        llm["pos"] = nh.pos
+        return
     h = _handle(llm)
     if h.pos + toks.size > int(llm["max_seq_len"]):
         raise RuntimeError("Sequence length exceeded")
@@ -543,6 +680,15 @@ def generate_embeddings(llm: dict[str, Any], input_array: Any) -> npt.NDArray[np
     max_len = max(len(r) for r in rows)
     if max_len == 0:
         raise RuntimeError("inputs must contain at least one token")
+    nh = _nano(llm)
+    if nh is not None:  # forward_nano_sequence per row (layers.mojo:1007-1063)
+        out = np.zeros((len(rows), int(llm["hidden_size"])), np.float32)
+        for i, r in enumerate(rows):
+            if not r:
+                raise RuntimeError("inputs must contain at least one token")
+            ids = _i32(r)
+            _check(_lib.mg_nano_embed(nh.ptr, ids.ctypes.data_as(_I32P), len(r), out[i].ctypes.data_as(_F32P)))
+        return _ensure_embedding_matrix(out, len(rows), int(llm["hidden_size"]))
     h = _handle(llm)
     ids = np.zeros((len(rows), max_len), np.int32)
     lens = np.zeros(len(rows), np.int32)

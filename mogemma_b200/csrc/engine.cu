@@ -727,6 +727,12 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
         const size_t n_tab = static_cast<size_t>(m->cap) * (hd / 2);
         TRY(dalloc(m, &m->cos_l, n_tab));
         TRY(dalloc(m, &m->sin_l, n_tab));
+        if (m->mode != 0) {
+            TRY(dalloc(m, &m->cos_g, n_tab));
+            TRY(dalloc(m, &m->sin_g, n_tab));
+        }
+        // the clears above run on the model's stream, which does not order with these synchronous copies
+        CU(cudaStreamSynchronize(m->stream));
         rope_table(c, s, m->cap, hd, m->mode == 0 ? 10000.f : m->theta_l);
         CU(cudaMemcpy(m->cos_l, c.data(), n_tab * 4, cudaMemcpyHostToDevice));
         CU(cudaMemcpy(m->sin_l, s.data(), n_tab * 4, cudaMemcpyHostToDevice));
@@ -734,8 +740,6 @@ static mg_status create_impl(const mg_tensor_desc *descs, int32_t n, const mg_op
             m->cos_g = m->cos_l;
             m->sin_g = m->sin_l;
         } else {
-            TRY(dalloc(m, &m->cos_g, n_tab));
-            TRY(dalloc(m, &m->sin_g, n_tab));
             rope_table(c, s, m->cap, hd, m->theta_g);
             CU(cudaMemcpy(m->cos_g, c.data(), n_tab * 4, cudaMemcpyHostToDevice));
             CU(cudaMemcpy(m->sin_g, s.data(), n_tab * 4, cudaMemcpyHostToDevice));

@@ -356,6 +356,8 @@ class AsyncGemmaModel:
         llm = self._model._llm  # noqa: SLF001
         if self._rows < 2 or core is None or not hasattr(core, "set_row_pos") or not isinstance(llm, dict):
             return None
+        if llm.get("arch") == "nano":  # the Gemma 3n engine decodes one stream: serial, as the reference
+            return None
         if self._scheduler is None:
             from .serving import BatchScheduler  # noqa: PLC0415
 
