@@ -198,6 +198,82 @@ def run_prefill(args, world: int, rank: int, local: int) -> None:
 EMBED_BATCH, EMBED_LEN, EMBED_DENSE = 256, (16, 512), 3072
 
 
+NANO_VOCAB = 32768  # the 262k-row per-layer table alone would be 8 GB of host and device memory
+
+
+def run_nano(args, world: int, rank: int, local: int) -> None:
+    """Gemma 3n decode tokens/s (mg_nano_*): a Gemma 3n E2B-like shape (hidden 2048, 30 layers, 8/2 heads of
+    256, FFN 8192, per-layer dim 256, Laurel rank 64, 4 AltUp streams, KV sharing from layer 20) with a
+    32,768-token vocabulary; fp32 weights tiled from one seeded random block (throughput does not depend on
+    the values).  --prompt tokens are prefilled, then --decode steps each return fp32 logits to the host (the
+    reference's step contract) and are timed by the host clock; every step synchronises.  Replicas for N > 1."""
+    from mogemma_b200 import _core, synth  # noqa: PLC0415
+
+    d = synth.NanoDims("gemma3n-e2b-shape", 2048, 30, 8, 2, 256, 8192, 256, 64, 4, NANO_VOCAB, kv_share_start=20)
+    block = (np.random.default_rng(0).standard_normal(1 << 20).astype(np.float32) * np.float32(0.02))
+    weights: dict[str, np.ndarray] = {}
+    for name, shape in synth.nano_tensor_shapes(d).items():
+        a = np.resize(block, shape)
+        if name.endswith("norm.weight") or name.endswith("output_scale"):
+            a = a + np.float32(1.0)
+        layer = int(name.split(".")[2]) if name.startswith("model.layers.") else -1
+        if layer >= 20 and (name.endswith("k_proj.weight") or name.endswith("v_proj.weight")):
+            a = np.zeros(shape, np.float32)
+        weights[name] = np.ascontiguousarray(a, np.float32)
+    weights["lm_head.weight"] = weights["model.embed_tokens.weight"]
+    # bytes one step reads: every tensor, except one row of the embedding and of the per-layer table, and no
+    # k/v projections of the layers that share an earlier layer's cache
+    step_bytes = 0
+    for name, a in weights.items():
+        if name == "model.embed_tokens.weight":
+            step_bytes += d.hidden * 4
+        elif name == "model.per_layer_embed.weight":
+            step_bytes += d.layers * d.per_layer_dim * 4
+        elif not ((name.endswith("k_proj.weight") or name.endswith("v_proj.weight")) and not a.any()):
+            step_bytes += a.nbytes
+    llm = _core.init_model(synth.metadata_of(weights), device=local, capacity=PROMPT + DECODE)
+    prompt = [int(t) for t in synth.prompt_ids(PROMPT, d.vocab, seed=1)]
+
+    def run() -> float:
+        llm["pos"] = 0
+        _core.prefill(llm, prompt[:-1])
+        cur = prompt[-1]
+        t0 = time.perf_counter()
+        for _ in range(DECODE):
+            logits = _core.step(llm, cur, 0.0, 0, 1.0)
+            cur = int(np.argmax(logits))
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        run()
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        dt = min(run() for _ in range(args.steps))
+    dt = dist_max(dt, world)
+    ms_tok = dt * 1e3 / DECODE
+    achieved = step_bytes / (ms_tok / 1e3) / 1e9
+    pk = peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Gemma 3n decode tokens/s (E2B-like shape, 32k vocabulary)", "value": world * DECODE / dt,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (weights tiled from one seeded N(0,0.02) block; random prompt ids)",
+            "config": {"workload": f"gemma3n E2B-like shape, {PROMPT}-token prompt then {DECODE} greedy tokens, "
+                                   "logits to the host every step (host clock)",
+                       "model": d.name, "global_batch": world, "seq_len": PROMPT + DECODE,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "e2e": {"value": world * DECODE / dt, "unit": "tokens/s", "h2d_bytes_per_step": 8 * DECODE,
+                    "d2h_bytes_per_step": 4 * d.vocab * DECODE},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"],
+                         "kernel": "nano step graph (one warp per GEMV row, single-CTA norms and AltUp)",
+                         "algorithmic_bytes_per_launch": step_bytes},
+            "cpu_baseline": None, "clocks": clocks.summary(),
+            "gpu_launches": DECODE * args.steps, "ms_per_token": ms_tok}), flush=True)
+    llm["_handle"].close()
+
+
 def run_embed(args, world: int, rank: int, local: int) -> None:
     """Sequences/s of the bidirectional encoder (mg_encode): EmbeddingGemma-style
     shape, 256 sequences with lengths uniform in [16, 512], dense 768->3072->768
@@ -428,7 +504,7 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1,
                     help="decode rows (beyond the rows one persistent launch holds: one launch per row group, "
                          "or the batched tensor-core steps with --batched-tc)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "embed"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "embed", "nano"],
                     help="prefill: the batched tensor-core prefill of --prompt tokens; embed: the bidirectional "
                          "encoder on 256 sequences")
     ap.add_argument("--embed-batch", type=int, default=EMBED_BATCH,
@@ -453,6 +529,9 @@ def main() -> None:
         return
     if args.workload == "embed":
         run_embed(args, world, rank, local)
+        return
+    if args.workload == "nano":
+        run_nano(args, world, rank, local)
         return
 
     import ctypes  # noqa: PLC0415
