@@ -39,9 +39,10 @@ def test_struct_layout_matches_header(tmp_path: Path) -> None:
     src = tmp_path / "sizes.c"
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "mogemma_b200.h"\n'
-        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(mg_tensor_desc), sizeof(mg_options),"
+        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(mg_tensor_desc), sizeof(mg_options),"
         " sizeof(mg_model_info), sizeof(mg_sampling), offsetof(mg_options, seed), offsetof(mg_options, reserved1),"
-        " offsetof(mg_sampling, uniforms_host), offsetof(mg_options, synthetic_seed)); return 0;}\n")
+        " offsetof(mg_sampling, uniforms_host), offsetof(mg_options, synthetic_seed), sizeof(mg_nano_info));"
+        " return 0;}\n")
     exe = tmp_path / "sizes"
     try:
         subprocess.run(["gcc", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
@@ -52,7 +53,7 @@ def test_struct_layout_matches_header(tmp_path: Path) -> None:
 
     want = [ctypes.sizeof(_core.TensorDesc), ctypes.sizeof(_core.Options), ctypes.sizeof(_core.ModelInfo),
             ctypes.sizeof(_core.Sampling), _core.Options.seed.offset, _core.Options.reserved1.offset,
-            _core.Sampling.uniforms_host.offset, _core.Options.synthetic_seed.offset]
+            _core.Sampling.uniforms_host.offset, _core.Options.synthetic_seed.offset, ctypes.sizeof(_core.NanoInfo)]
     assert got == want
 
 
@@ -63,3 +64,16 @@ def test_create_without_tensors_fails_cleanly() -> None:
     st = _core.lib().mg_model_create(None, 0, None, ctypes.byref(out))
     assert st == _core.MG_ERR_INVALID
     assert b"no tensors" in _core.lib().mg_last_error()
+
+
+def test_nano_create_rejects_bad_input_without_a_device() -> None:
+    """mg_nano_create checks its arguments and the checkpoint kind before any CUDA call."""
+    import ctypes  # noqa: PLC0415
+
+    out = ctypes.c_void_p()
+    lib = _core.lib()
+    assert lib.mg_nano_create(None, 0, 0, 64, ctypes.byref(out)) == _core.MG_ERR_INVALID
+    descs, _keep = _core._tensor_descs({"model.embed_tokens.weight": (1, (4, 2), "F32")})  # noqa: SLF001
+    assert lib.mg_nano_create(descs, len(descs), 0, 64, ctypes.byref(out)) == _core.MG_ERR_INVALID
+    assert b"not a Gemma 3n checkpoint" in lib.mg_last_error()
+    assert not out.value
